@@ -1,0 +1,286 @@
+// Expert-parallel dispatch / combine around NCCL all-to-all.
+//
+// The reference's cross-DP backends all-gather every replica's tokens, route
+// the global batch on every rank and reduce the [N*T, H] partial outputs
+// (nanovllm/layers/moe.py:942-1018).  Here each rank routes only its own
+// tokens and exchanges:
+//   dispatch: every token once per destination rank that owns at least one
+//             of its kept routes, plus 16-byte route records
+//             {expert, token row at the destination, weight, source route};
+//   return:   one bf16 row per kept route, in the order it was received, so
+//             the source combines its routes in slot order exactly as with
+//             EP=1 (moe.py:642-678).
+// These kernels build the plan (per-destination slots), pack the payload and
+// translate received records; the all-to-all itself is NCCL.
+#include "common.cuh"
+
+namespace b200moe {
+namespace {
+
+constexpr int kMaxEp = 16;
+constexpr int kPlanThreads = 1024;
+
+struct Offsets {
+  int32_t v[kMaxEp + 1];
+};
+
+__device__ __forceinline__ int dest_of(int64_t id, int num_experts, const int32_t *owner,
+                                       int ep_size) {
+  if (id < 0 || id >= num_experts) return -1;
+  const int d = owner[id];
+  return (d >= 0 && d < ep_size) ? d : -1;
+}
+
+// Exclusive scan of each column d of sh[kPlanThreads][N] in place; warp d owns
+// column d, each lane a run of kPlanThreads / 32 consecutive rows.
+__device__ void scan_columns(int32_t *sh, int N, int32_t *totals) {
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= N) return;
+  constexpr int kPer = kPlanThreads / 32;
+  int32_t sum = 0;
+  for (int i = 0; i < kPer; ++i) sum += sh[(lane * kPer + i) * N + warp];
+  int32_t incl = sum;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int32_t v = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += v;
+  }
+  int32_t run = incl - sum;
+  for (int i = 0; i < kPer; ++i) {
+    const int idx = (lane * kPer + i) * N + warp;
+    const int32_t c = sh[idx];
+    sh[idx] = run;
+    run += c;
+  }
+  if (lane == 31) totals[warp] = incl;
+}
+
+// Single CTA: ordered slots per destination for tokens and routes.
+__global__ void __launch_bounds__(kPlanThreads) ep_plan_kernel(
+    const int64_t *__restrict__ ids, int64_t num_tokens, int top_k, int num_experts,
+    const int32_t *__restrict__ owner, int ep_size, int32_t *__restrict__ send_token_slot,
+    int32_t *__restrict__ route_dest_slot, int32_t *__restrict__ counts) {
+  extern __shared__ int32_t sh[];  // [kPlanThreads][ep_size] scan buffer
+  const int tid = threadIdx.x;
+  const int N = ep_size;
+  const int64_t T = num_tokens;
+  const int64_t R = num_tokens * top_k;
+  // Pass A: routes.  Thread tid owns routes [r0, r1).
+  {
+    const int64_t per = (R + kPlanThreads - 1) / kPlanThreads;
+    const int64_t r0 = min(R, tid * per), r1 = min(R, r0 + per);
+    int32_t local[kMaxEp];
+    for (int d = 0; d < N; ++d) local[d] = 0;
+    for (int64_t r = r0; r < r1; ++r) {
+      const int d = dest_of(ids[r], num_experts, owner, N);
+      if (d >= 0) ++local[d];
+    }
+    for (int d = 0; d < N; ++d) sh[tid * N + d] = local[d];
+    __syncthreads();
+    scan_columns(sh, N, counts + N);
+    __syncthreads();
+    for (int d = 0; d < N; ++d) local[d] = sh[tid * N + d];
+    for (int64_t r = r0; r < r1; ++r) {
+      const int d = dest_of(ids[r], num_experts, owner, N);
+      route_dest_slot[r] = d >= 0 ? local[d]++ : -1;
+    }
+    __syncthreads();
+  }
+  // Pass B: tokens.
+  {
+    const int64_t per = (T + kPlanThreads - 1) / kPlanThreads;
+    const int64_t t0 = min(T, tid * per), t1 = min(T, t0 + per);
+    int32_t local[kMaxEp];
+    for (int d = 0; d < N; ++d) local[d] = 0;
+    for (int64_t t = t0; t < t1; ++t) {
+      uint64_t mask = 0;
+      for (int s = 0; s < top_k; ++s) {
+        const int d = dest_of(ids[t * top_k + s], num_experts, owner, N);
+        if (d >= 0) mask |= 1ull << d;
+      }
+      for (int d = 0; d < N; ++d) local[d] += (mask >> d) & 1;
+    }
+    for (int d = 0; d < N; ++d) sh[tid * N + d] = local[d];
+    __syncthreads();
+    scan_columns(sh, N, counts);
+    __syncthreads();
+    for (int d = 0; d < N; ++d) local[d] = sh[tid * N + d];
+    for (int64_t t = t0; t < t1; ++t) {
+      uint64_t mask = 0;
+      for (int s = 0; s < top_k; ++s) {
+        const int d = dest_of(ids[t * top_k + s], num_experts, owner, N);
+        if (d >= 0) mask |= 1ull << d;
+      }
+      for (int d = 0; d < N; ++d)
+        send_token_slot[t * N + d] = ((mask >> d) & 1) ? local[d]++ : -1;
+    }
+  }
+}
+
+// One warp per token: copy its row to every destination slot, then write the
+// records of its routes.
+__global__ void __launch_bounds__(256) ep_pack_kernel(
+    const __nv_bfloat16 *__restrict__ x, int hidden, const int64_t *__restrict__ ids,
+    const __nv_bfloat16 *__restrict__ rw, int64_t num_tokens, int top_k, int num_experts,
+    const int32_t *__restrict__ owner, int ep_size, const int32_t *__restrict__ send_token_slot,
+    const int32_t *__restrict__ route_dest_slot, Offsets tok_off, Offsets route_off,
+    __nv_bfloat16 *__restrict__ send_x, int4 *__restrict__ send_meta) {
+  const int lane = threadIdx.x & 31;
+  const int64_t t = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (t >= num_tokens) return;
+  const int vecs = hidden / 8;
+  const uint4 *src = reinterpret_cast<const uint4 *>(x + t * hidden);
+  for (int d = 0; d < ep_size; ++d) {
+    const int32_t slot = send_token_slot[t * ep_size + d];
+    if (slot < 0) continue;
+    uint4 *dst = reinterpret_cast<uint4 *>(send_x + static_cast<int64_t>(tok_off.v[d] + slot) * hidden);
+    for (int v = lane; v < vecs; v += 32) dst[v] = src[v];
+  }
+  if (lane < top_k) {
+    const int64_t r = t * top_k + lane;
+    const int64_t id = ids[r];
+    const int d = dest_of(id, num_experts, owner, ep_size);
+    const int32_t slot = route_dest_slot[r];
+    if (d >= 0 && slot >= 0) {
+      const uint16_t wbits = __bfloat16_as_ushort(rw[r]);
+      send_meta[route_off.v[d] + slot] =
+          make_int4(static_cast<int>(id), send_token_slot[t * ep_size + d], static_cast<int>(wbits),
+                    static_cast<int>(r));
+    }
+  }
+}
+
+__global__ void ep_unpack_kernel(const int4 *__restrict__ meta, int64_t n, int ep_size,
+                                 Offsets recv_route_off, Offsets recv_tok_off,
+                                 int64_t *__restrict__ ids, int32_t *__restrict__ token_of_route,
+                                 __nv_bfloat16 *__restrict__ rw) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  int src = 0;
+  while (src + 1 < ep_size && i >= recv_route_off.v[src + 1]) ++src;
+  const int4 m = meta[i];
+  ids[i] = m.x;
+  token_of_route[i] = recv_tok_off.v[src] + m.y;
+  rw[i] = __ushort_as_bfloat16(static_cast<unsigned short>(m.z & 0xffff));
+}
+
+__global__ void ep_return_rows_kernel(const int64_t *__restrict__ ids,
+                                      const int32_t *__restrict__ owner, int64_t num_routes,
+                                      int num_experts, int ep_size,
+                                      const int32_t *__restrict__ route_dest_slot, Offsets route_off,
+                                      int64_t num_rows_returned, int32_t *__restrict__ combine_rows) {
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (r >= num_routes) return;
+  const int d = dest_of(ids[r], num_experts, owner, ep_size);
+  const int32_t slot = route_dest_slot[r];
+  combine_rows[r] = (d >= 0 && slot >= 0) ? route_off.v[d] + slot
+                                          : static_cast<int32_t>(num_rows_returned);
+}
+
+int load_offsets(Offsets &o, const int32_t *host, int n) {
+  for (int i = 0; i <= kMaxEp; ++i) o.v[i] = 0;
+  for (int i = 0; i < n; ++i) o.v[i] = host[i];
+  return B200MOE_OK;
+}
+
+}  // namespace
+}  // namespace b200moe
+
+extern "C" {
+
+int b200moe_ep_plan(const int64_t *expert_ids, int64_t num_tokens, int top_k, int num_experts,
+                    const int32_t *owner, int ep_size, int32_t *send_token_slot,
+                    int32_t *route_dest_slot, int32_t *counts, void *stream) {
+  using namespace b200moe;
+  B200_ARG(ep_size >= 1 && ep_size <= kMaxEp, "ep_size must be in [1, %d]", kMaxEp);
+  B200_ARG(num_tokens >= 0 && top_k >= 1 && num_experts >= 1, "bad shape");
+  B200_ARG(owner && counts, "null pointer argument");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (num_tokens == 0) {
+    B200_CUDA(cudaMemsetAsync(counts, 0, sizeof(int32_t) * 2 * ep_size, s));
+    return B200MOE_OK;
+  }
+  B200_ARG(expert_ids && send_token_slot && route_dest_slot, "null pointer argument");
+  const size_t smem = sizeof(int32_t) * kPlanThreads * ep_size;
+  if (smem > 48 * 1024)
+    B200_CUDA(cudaFuncSetAttribute(ep_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(smem)));
+  ep_plan_kernel<<<1, kPlanThreads, smem, s>>>(expert_ids, num_tokens, top_k, num_experts, owner,
+                                               ep_size, send_token_slot, route_dest_slot, counts);
+  B200_LAUNCHED();
+  return B200MOE_OK;
+}
+
+int b200moe_ep_pack(const void *x, int hidden, const int64_t *expert_ids,
+                    const void *route_weights, int64_t num_tokens, int top_k, int num_experts,
+                    const int32_t *owner, int ep_size, const int32_t *send_token_slot,
+                    const int32_t *route_dest_slot, const int32_t *token_offsets_host,
+                    const int32_t *route_offsets_host, void *send_x, int32_t *send_meta,
+                    void *stream) {
+  using namespace b200moe;
+  B200_ARG(ep_size >= 1 && ep_size <= kMaxEp, "ep_size must be in [1, %d]", kMaxEp);
+  B200_UNSUPPORTED(hidden % 8 == 0, "hidden must be a multiple of 8");
+  B200_ARG(top_k >= 1 && top_k <= 32, "top_k must be in [1, 32]");
+  if (num_tokens == 0) return B200MOE_OK;
+  B200_ARG(x && expert_ids && route_weights && owner && send_token_slot && route_dest_slot &&
+               token_offsets_host && route_offsets_host,
+           "null pointer argument");
+  Offsets to, ro;
+  load_offsets(to, token_offsets_host, ep_size);
+  load_offsets(ro, route_offsets_host, ep_size);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t blocks = (num_tokens * 32 + 255) / 256;
+  ep_pack_kernel<<<blocks, 256, 0, s>>>(
+      static_cast<const __nv_bfloat16 *>(x), hidden, expert_ids,
+      static_cast<const __nv_bfloat16 *>(route_weights), num_tokens, top_k, num_experts, owner,
+      ep_size, send_token_slot, route_dest_slot, to, ro, static_cast<__nv_bfloat16 *>(send_x),
+      reinterpret_cast<int4 *>(send_meta));
+  B200_LAUNCHED();
+  return B200MOE_OK;
+}
+
+int b200moe_ep_unpack_routes(const int32_t *recv_meta, int64_t num_recv_routes, int ep_size,
+                             const int32_t *recv_route_offsets_host,
+                             const int32_t *recv_token_offsets_host, int64_t *expert_ids,
+                             int32_t *token_of_route, void *route_weights, void *stream) {
+  using namespace b200moe;
+  B200_ARG(ep_size >= 1 && ep_size <= kMaxEp, "ep_size must be in [1, %d]", kMaxEp);
+  if (num_recv_routes == 0) return B200MOE_OK;
+  B200_ARG(recv_meta && recv_route_offsets_host && recv_token_offsets_host && expert_ids &&
+               token_of_route && route_weights,
+           "null pointer argument");
+  Offsets ro, to;
+  load_offsets(ro, recv_route_offsets_host, ep_size + 1);
+  load_offsets(to, recv_token_offsets_host, ep_size);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t blocks = (num_recv_routes + 255) / 256;
+  ep_unpack_kernel<<<blocks, 256, 0, s>>>(reinterpret_cast<const int4 *>(recv_meta),
+                                          num_recv_routes, ep_size, ro, to, expert_ids,
+                                          token_of_route,
+                                          static_cast<__nv_bfloat16 *>(route_weights));
+  B200_LAUNCHED();
+  return B200MOE_OK;
+}
+
+int b200moe_ep_return_rows(const int64_t *expert_ids, const int32_t *owner, int64_t num_routes,
+                           int num_experts, int ep_size, const int32_t *route_dest_slot,
+                           const int32_t *route_offsets_host, int64_t num_rows_returned,
+                           int32_t *combine_rows, void *stream) {
+  using namespace b200moe;
+  B200_ARG(ep_size >= 1 && ep_size <= kMaxEp, "ep_size must be in [1, %d]", kMaxEp);
+  if (num_routes == 0) return B200MOE_OK;
+  B200_ARG(expert_ids && owner && route_dest_slot && route_offsets_host && combine_rows,
+           "null pointer argument");
+  Offsets ro;
+  load_offsets(ro, route_offsets_host, ep_size);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t blocks = (num_routes + 255) / 256;
+  ep_return_rows_kernel<<<blocks, 256, 0, s>>>(expert_ids, owner, num_routes, num_experts,
+                                               ep_size, route_dest_slot, ro, num_rows_returned,
+                                               combine_rows);
+  B200_LAUNCHED();
+  return B200MOE_OK;
+}
+
+}  // extern "C"

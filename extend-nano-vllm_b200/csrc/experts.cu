@@ -1,0 +1,81 @@
+// C entry points of the grouped expert projections: argument checks and the
+// choice between the weight-streaming engine (small decode buckets) and the
+// tcgen05 grouped GEMM (prefill and larger buckets).
+#include "common.cuh"
+
+namespace b200moe {
+int stream_gate_up(const void *x, int64_t x_rows, int hidden, int inter, const void *w13,
+                   const int32_t *row_route, const int32_t *token_of_route, int top_k,
+                   int64_t num_routes, const int32_t *mtiles, int64_t max_mtiles,
+                   const int32_t *counters, void *act, cudaStream_t s);
+int stream_down(const void *act, int hidden, int inter, const void *w2, const int32_t *row_route,
+                const void *route_weights, int64_t num_routes, const int32_t *mtiles,
+                int64_t max_mtiles, const int32_t *counters, void *y, cudaStream_t s);
+int tc_gate_up(const void *x_packed, int hidden, int inter, const void *w13, int num_local,
+               int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
+               const int32_t *counters, void *act, cudaStream_t s);
+int tc_down(const void *act, int hidden, int inter, const void *w2, int num_local,
+            const int32_t *row_route, const void *route_weights, int64_t num_routes,
+            int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
+            const int32_t *counters, void *y, cudaStream_t s);
+
+namespace {
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+}  // namespace
+}  // namespace b200moe
+
+extern "C" {
+
+int b200moe_expert_gate_up(int engine, const void *x, int64_t x_rows, const void *x_packed,
+                           int hidden, int inter, const void *w13, int num_local_experts,
+                           const int32_t *row_route, const int32_t *token_of_route, int top_k,
+                           int64_t num_routes, int64_t row_capacity, const int32_t *mtiles,
+                           int64_t max_mtiles, const int32_t *counters, void *act,
+                           void *stream) {
+  using namespace b200moe;
+  B200_ARG(hidden > 0 && inter > 0 && num_local_experts > 0 && top_k > 0, "bad shape");
+  B200_UNSUPPORTED(hidden % 16 == 0 && inter % 16 == 0,
+                   "hidden (%d) and intermediate (%d) sizes must be multiples of 16", hidden, inter);
+  if (num_routes == 0 || max_mtiles == 0) return B200MOE_OK;
+  B200_ARG(w13 && row_route && mtiles && counters && act, "null pointer argument");
+  B200_ARG(aligned16(w13) && aligned16(act), "w13 and act must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (engine == B200MOE_ENGINE_STREAM) {
+    B200_ARG(x != nullptr && aligned16(x), "x must be a 16-byte aligned device pointer");
+    return stream_gate_up(x, x_rows, hidden, inter, w13, row_route, token_of_route, top_k,
+                          num_routes, mtiles, max_mtiles, counters, act, s);
+  }
+  if (engine == B200MOE_ENGINE_TCGEN05) {
+    B200_ARG(x_packed != nullptr && aligned16(x_packed), "x_packed must be 16-byte aligned");
+    return tc_gate_up(x_packed, hidden, inter, w13, num_local_experts, row_capacity, mtiles,
+                      max_mtiles, counters, act, s);
+  }
+  set_error("unknown engine %d", engine);
+  return B200MOE_EINVAL;
+}
+
+int b200moe_expert_down(int engine, const void *act, int hidden, int inter, const void *w2,
+                        int num_local_experts, const int32_t *row_route,
+                        const void *route_weights, int64_t num_routes, int64_t row_capacity,
+                        const int32_t *mtiles, int64_t max_mtiles, const int32_t *counters,
+                        void *y, void *stream) {
+  using namespace b200moe;
+  B200_ARG(hidden > 0 && inter > 0 && num_local_experts > 0, "bad shape");
+  B200_UNSUPPORTED(hidden % 16 == 0 && inter % 16 == 0,
+                   "hidden (%d) and intermediate (%d) sizes must be multiples of 16", hidden, inter);
+  if (num_routes == 0 || max_mtiles == 0) return B200MOE_OK;
+  B200_ARG(act && w2 && row_route && route_weights && mtiles && counters && y,
+           "null pointer argument");
+  B200_ARG(aligned16(act) && aligned16(w2) && aligned16(y), "act, w2, y must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (engine == B200MOE_ENGINE_STREAM)
+    return stream_down(act, hidden, inter, w2, row_route, route_weights, num_routes, mtiles,
+                       max_mtiles, counters, y, s);
+  if (engine == B200MOE_ENGINE_TCGEN05)
+    return tc_down(act, hidden, inter, w2, num_local_experts, row_route, route_weights,
+                   num_routes, row_capacity, mtiles, max_mtiles, counters, y, s);
+  set_error("unknown engine %d", engine);
+  return B200MOE_EINVAL;
+}
+
+}  // extern "C"

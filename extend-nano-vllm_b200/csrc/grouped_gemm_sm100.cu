@@ -1,0 +1,402 @@
+// Grouped expert GEMMs on the 5th-generation tensor cores (tcgen05 + TMEM),
+// fed by TMA, for prefill and the larger decode buckets (engine TCGEN05).
+//
+// Replaces the reference Triton _grouped_moe_gemm_kernel
+// (nanovllm/layers/moe.py:63-139: one program per 16-row tile x 64 columns,
+// K step 32) and the separate SwiGLU (moe.py:853-854).  Design:
+//  * Work = (128-row tile of one expert's packed rows) x (256-column tile of
+//    its weights).  The tile list comes from b200moe_pack_routes on the device,
+//    so inactive experts cost nothing and no host sync is needed; the grid is
+//    persistent (one CTA per SM) and walks the list with a static stride.
+//  * Warp 0 issues TMA loads (A: 128 x 64 activation rows, B: 256 x 64 weight
+//    rows, 128-byte swizzle) into a 4-stage mbarrier ring; warp 1 issues
+//    tcgen05.mma (M=128, N=256, K=16) into one of two TMEM accumulators
+//    (2 x 256 fp32 columns); warps 2-5 drain the other accumulator with
+//    tcgen05.ld and run the epilogue, so the epilogue of tile i overlaps the
+//    MMAs of tile i+1.
+//  * gate/up: the 256 B rows are 128 gate rows and the matching 128 up rows
+//    (two TMA boxes of a [2E, I, H] view of W13), so each thread holds gate
+//    and up of the same feature and applies SwiGLU in registers with the
+//    reference's bf16 rounding points, writing act in packed order.
+//  * down: the epilogue scales the fp32 accumulator by the route weight before
+//    the bf16 store (moe.py:129-139) and writes rows in route order.
+// Every mbarrier wait is bounded (2 s of global time); on expiry the CTA
+// records the timeout in the status word, all roles leave their loops and
+// TMEM is released before the kernel returns.
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+
+namespace b200moe {
+namespace tcg {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;
+constexpr int B_BYTES = BN * BK * 2;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int TMEM_COLS = 2 * BN;
+constexpr int THREADS = 192;
+constexpr size_t SMEM_BYTES = 1024 + static_cast<size_t>(STAGES) * STAGE_BYTES + 256;
+
+struct Args {
+  const int32_t *mtiles;
+  const int32_t *counters;
+  int64_t max_mtiles;
+  int n_tiles;  // column tiles per row tile
+  int num_kb;   // K blocks of 64
+  int n_out;    // output columns: I (gate/up) or H (down)
+  __nv_bfloat16 *out;
+  const int32_t *row_route;
+  const __nv_bfloat16 *route_w;
+  int64_t num_routes;
+};
+
+__device__ __forceinline__ void store16_bf16(__nv_bfloat16 *dst, const float (&v)[16], int valid) {
+  if (valid >= 16) {
+    uint4 o[2];
+    __nv_bfloat162 *op = reinterpret_cast<__nv_bfloat162 *>(o);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) op[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+    reinterpret_cast<uint4 *>(dst)[0] = o[0];
+    reinterpret_cast<uint4 *>(dst)[1] = o[1];
+  } else {
+    for (int i = 0; i < valid; ++i) dst[i] = __float2bfloat16_rn(v[i]);
+  }
+}
+
+template <bool kGateUp>
+__global__ void __launch_bounds__(THREADS, 1)
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
+                        const __grid_constant__ CUtensorMap tmB, const Args args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~static_cast<uintptr_t>(1023));
+  uint8_t *sA = smem;
+  uint8_t *sB = smem + STAGES * A_BYTES;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sB + STAGES * B_BYTES);
+  uint64_t *full = bars;
+  uint64_t *empty = bars + STAGES;
+  uint64_t *acc_full = bars + 2 * STAGES;
+  uint64_t *acc_empty = bars + 2 * STAGES + 2;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 4);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_mtiles =
+      static_cast<int>(min64(args.counters[B200MOE_CNT_MTILES], args.max_mtiles));
+  const int num_work = num_mtiles * args.n_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&acc_full[a]), 1);
+      mbar_init(smem_u32(&acc_empty[a]), 4);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_holder), TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; w < num_work && ok; w += gridDim.x) {
+        const int m = w / args.n_tiles;
+        const int n = w - m * args.n_tiles;
+        const int e = args.mtiles[m * B200MOE_MTILE_WORDS + 0];
+        const int rb = args.mtiles[m * B200MOE_MTILE_WORDS + 1];
+        for (int kb = 0; kb < args.num_kb; ++kb) {
+          if (!mbar_wait_bounded(smem_u32(&empty[stage]), phase ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(&full[stage]);
+          mbar_arrive_expect_tx(fb, STAGE_BYTES);
+          tma_load_2d(smem_u32(sA + stage * A_BYTES), &tmA, fb, kb * BK, rb);
+          if (kGateUp) {
+            tma_load_3d(smem_u32(sB + stage * B_BYTES), &tmB, fb, kb * BK, n * (BN / 2), 2 * e);
+            tma_load_3d(smem_u32(sB + stage * B_BYTES + B_BYTES / 2), &tmB, fb, kb * BK,
+                        n * (BN / 2), 2 * e + 1);
+          } else {
+            tma_load_3d(smem_u32(sB + stage * B_BYTES), &tmB, fb, kb * BK, n * BN, e);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; w < num_work && ok; w += gridDim.x) {
+        if (!mbar_wait_bounded(smem_u32(&acc_empty[acc]), acc_phase ^ 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < args.num_kb; ++kb) {
+          if (!mbar_wait_bounded(smem_u32(&full[stage]), phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b0 = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            tc_mma_f16(d_tmem, sw128_kmajor_desc(a0 + kk * 32), sw128_kmajor_desc(b0 + kk * 32),
+                       idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          tc_commit(smem_u32(&empty[stage]));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit(smem_u32(&acc_full[acc]));
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int w = blockIdx.x; w < num_work; w += gridDim.x) {
+      const int m = w / args.n_tiles;
+      const int n = w - m * args.n_tiles;
+      const int rb = args.mtiles[m * B200MOE_MTILE_WORDS + 1];
+      const int re = args.mtiles[m * B200MOE_MTILE_WORDS + 2];
+      if (!mbar_wait_bounded(smem_u32(&acc_full[acc]), acc_phase, abort_flag)) break;
+      tc_fence_after();
+      const int row = rb + q * 32 + lane;
+      const bool valid = row < re;
+      const uint32_t taddr =
+          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      if (kGateUp) {
+        const int col0 = n * (BN / 2);
+        __nv_bfloat16 *dst_row = args.out + static_cast<int64_t>(row) * args.n_out;
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 16) {
+          float g[16], u[16];
+          tmem_ld16(taddr + c, g);
+          tmem_ld16(taddr + BN / 2 + c, u);
+          tmem_ld_wait();
+          const int cols = args.n_out - (col0 + c);
+          if (valid && cols > 0) {
+            float a[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) a[i] = swiglu_bf16(g[i], u[i]);
+            store16_bf16(dst_row + col0 + c, a, cols);
+          }
+        }
+      } else {
+        int32_t route = -1;
+        float rw = 0.f;
+        if (valid) {
+          route = args.row_route[row];
+          if (route < 0 || route >= args.num_routes) {
+            atomicOr(&g_status, kStatusIndex);
+            route = -1;
+          } else {
+            rw = __bfloat162float(args.route_w[route]);
+          }
+        }
+        const int col0 = n * BN;
+        __nv_bfloat16 *dst_row =
+            args.out + static_cast<int64_t>(route < 0 ? 0 : route) * args.n_out;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          float v[16];
+          tmem_ld16(taddr + c, v);
+          tmem_ld_wait();
+          const int cols = args.n_out - (col0 + c);
+          if (route >= 0 && cols > 0) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] *= rw;
+            store16_bf16(dst_row + col0 + c, v, cols);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&acc_empty[acc]));
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ----------------------------------------------------------------------------
+// Host side: tensor maps and launch.
+// ----------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+int make_map(CUtensorMap *map, const void *base, int rank, const uint64_t *dims,
+             const uint64_t *strides_bytes, const uint32_t *box) {
+  auto fn = encode_fn();
+  if (fn == nullptr) {
+    set_error("cuTensorMapEncodeTiled is unavailable from the CUDA driver");
+    return B200MOE_ECUDA;
+  }
+  cuuint64_t d[3];
+  cuuint64_t st[2];
+  cuuint32_t bx[3];
+  cuuint32_t es[3] = {1, 1, 1};
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    bx[i] = box[i];
+  }
+  for (int i = 0; i + 1 < rank; ++i) st[i] = strides_bytes[i];
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<cuuint32_t>(rank),
+                        const_cast<void *>(base), d, st, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed with CUresult %d", static_cast<int>(r));
+    return B200MOE_ECUDA;
+  }
+  return B200MOE_OK;
+}
+
+template <bool kGateUp>
+int prepare_kernel() {
+  static bool done[64] = {false};
+  const int dev = current_device();
+  if (dev >= 0 && dev < 64 && done[dev]) return B200MOE_OK;
+  B200_CUDA(cudaFuncSetAttribute(grouped_gemm_kernel<kGateUp>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(SMEM_BYTES)));
+  if (dev >= 0 && dev < 64) done[dev] = true;
+  return B200MOE_OK;
+}
+
+template <bool kGateUp>
+int launch(const CUtensorMap &ma, const CUtensorMap &mb, const Args &args, cudaStream_t s) {
+  int rc = prepare_kernel<kGateUp>();
+  if (rc != B200MOE_OK) return rc;
+  int64_t work = args.max_mtiles * args.n_tiles;
+  int grid = sm_count();
+  if (work < grid) grid = static_cast<int>(work);
+  if (grid < 1) grid = 1;
+  grouped_gemm_kernel<kGateUp><<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb, args);
+  B200_LAUNCHED();
+  return B200MOE_OK;
+}
+
+}  // namespace tcg
+
+int tc_gate_up(const void *x_packed, int hidden, int inter, const void *w13, int num_local,
+               int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
+               const int32_t *counters, void *act, cudaStream_t s) {
+  using namespace tcg;
+  CUtensorMap ma, mb;
+  const uint64_t da[2] = {static_cast<uint64_t>(hidden), static_cast<uint64_t>(row_capacity)};
+  const uint64_t sa[1] = {static_cast<uint64_t>(hidden) * 2};
+  const uint32_t ba[2] = {BK, BM};
+  int rc = make_map(&ma, x_packed, 2, da, sa, ba);
+  if (rc) return rc;
+  const uint64_t db[3] = {static_cast<uint64_t>(hidden), static_cast<uint64_t>(inter),
+                          static_cast<uint64_t>(2) * num_local};
+  const uint64_t sb[2] = {static_cast<uint64_t>(hidden) * 2,
+                          static_cast<uint64_t>(inter) * hidden * 2};
+  const uint32_t bb[3] = {BK, BN / 2, 1};
+  rc = make_map(&mb, w13, 3, db, sb, bb);
+  if (rc) return rc;
+  Args a;
+  a.mtiles = mtiles;
+  a.counters = counters;
+  a.max_mtiles = max_mtiles;
+  a.n_tiles = (inter + BN / 2 - 1) / (BN / 2);
+  a.num_kb = (hidden + BK - 1) / BK;
+  a.n_out = inter;
+  a.out = static_cast<__nv_bfloat16 *>(act);
+  a.row_route = nullptr;
+  a.route_w = nullptr;
+  a.num_routes = 0;
+  return launch<true>(ma, mb, a, s);
+}
+
+int tc_down(const void *act, int hidden, int inter, const void *w2, int num_local,
+            const int32_t *row_route, const void *route_weights, int64_t num_routes,
+            int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
+            const int32_t *counters, void *y, cudaStream_t s) {
+  using namespace tcg;
+  CUtensorMap ma, mb;
+  const uint64_t da[2] = {static_cast<uint64_t>(inter), static_cast<uint64_t>(row_capacity)};
+  const uint64_t sa[1] = {static_cast<uint64_t>(inter) * 2};
+  const uint32_t ba[2] = {BK, BM};
+  int rc = make_map(&ma, act, 2, da, sa, ba);
+  if (rc) return rc;
+  const uint64_t db[3] = {static_cast<uint64_t>(inter), static_cast<uint64_t>(hidden),
+                          static_cast<uint64_t>(num_local)};
+  const uint64_t sb[2] = {static_cast<uint64_t>(inter) * 2,
+                          static_cast<uint64_t>(hidden) * inter * 2};
+  const uint32_t bb[3] = {BK, BN, 1};
+  rc = make_map(&mb, w2, 3, db, sb, bb);
+  if (rc) return rc;
+  Args a;
+  a.mtiles = mtiles;
+  a.counters = counters;
+  a.max_mtiles = max_mtiles;
+  a.n_tiles = (hidden + BN - 1) / BN;
+  a.num_kb = (inter + BK - 1) / BK;
+  a.n_out = hidden;
+  a.out = static_cast<__nv_bfloat16 *>(y);
+  a.row_route = row_route;
+  a.route_w = static_cast<const __nv_bfloat16 *>(route_weights);
+  a.num_routes = num_routes;
+  return launch<false>(ma, mb, a, s);
+}
+
+}  // namespace b200moe

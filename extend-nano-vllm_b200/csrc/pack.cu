@@ -1,0 +1,437 @@
+// Capacity keep-mask + expert-major packing (compact expert tasks), graph-safe.
+//
+// Reference behaviour reproduced bit-exactly:
+//  * capacity positions: stable order of the flat (token-major, slot-minor)
+//    routes within each expert; keep = position < capacity; dropped routes get
+//    id = num_experts and weight 0 (nanovllm/layers/moe.py:879-919);
+//  * local-route mapping for contiguous or explicit placements
+//    (moe.py:491-517, Triton _map_expert_routes_kernel moe.py:142-161);
+//  * expert-major packing with each expert's group padded to 16 rows, packed
+//    starts in local-expert order, route ids per packed row, one expert id per
+//    16-row tile, the device-side padded length (moe.py:790-847), and the
+//    route -> packed-row map of the dynamic path (moe.py:698-740, :763-767).
+//
+// Two kernels, no host synchronisation:
+//  1. pack_hist:    per-block expert histograms of contiguous route chunks
+//                   (scratch), plus sentinel fills of the outputs;
+//  2. pack_scatter: every block prefixes the histograms of the blocks before
+//                   it, recomputes the local-expert layout, then ranks its own
+//                   routes in order (warp match + per-warp counts) and scatters.
+#include "common.cuh"
+
+namespace b200moe {
+namespace {
+
+constexpr int kPackThreads = 256;
+constexpr int kPackWarps = kPackThreads / 32;
+
+__device__ __forceinline__ uint32_t lanemask_lt() {
+  uint32_t m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
+
+struct PackGeometry {
+  int64_t chunk;
+  int nblk;
+};
+
+PackGeometry pack_geometry(int64_t num_routes) {
+  PackGeometry g;
+  g.chunk = 1024;
+  int64_t nblk = (num_routes + g.chunk - 1) / g.chunk;
+  if (nblk > 512) {
+    g.chunk = ((num_routes + 511) / 512 + kPackThreads - 1) / kPackThreads * kPackThreads;
+    nblk = (num_routes + g.chunk - 1) / g.chunk;
+  }
+  g.nblk = static_cast<int>(nblk < 1 ? 1 : nblk);
+  return g;
+}
+
+__device__ __forceinline__ int route_key(int64_t id, int num_experts) {
+  return (id >= 0 && id < num_experts) ? static_cast<int>(id) : num_experts;
+}
+
+__global__ void __launch_bounds__(kPackThreads) pack_hist_kernel(
+    const int64_t *__restrict__ ids, int64_t num_routes, int num_experts, int64_t chunk,
+    int32_t *__restrict__ hist, int32_t *__restrict__ row_route, int64_t row_capacity,
+    int32_t *__restrict__ tile_expert, int32_t *__restrict__ counters) {
+  extern __shared__ int32_t sh_hist[];
+  const int E1 = num_experts + 1;
+  for (int e = threadIdx.x; e < E1; e += blockDim.x) sh_hist[e] = 0;
+  __syncthreads();
+  const int64_t begin = blockIdx.x * chunk;
+  const int64_t end = min(num_routes, begin + chunk);
+  for (int64_t r = begin + threadIdx.x; r < end; r += blockDim.x)
+    atomicAdd(&sh_hist[route_key(ids[r], num_experts)], 1);
+  __syncthreads();
+  for (int e = threadIdx.x; e < E1; e += blockDim.x)
+    hist[static_cast<int64_t>(blockIdx.x) * E1 + e] = sh_hist[e];
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int32_t sentinel = static_cast<int32_t>(num_routes);
+  for (int64_t i = first; i < row_capacity; i += stride) row_route[i] = sentinel;
+  for (int64_t i = first; i < row_capacity / B200MOE_BLOCK_ROWS; i += stride) tile_expert[i] = 0;
+  if (first < B200MOE_NUM_COUNTERS) counters[first] = 0;
+}
+
+struct ScatterArgs {
+  int64_t *ids;
+  __nv_bfloat16 *weights;
+  int64_t num_routes;
+  int num_experts;
+  const int64_t *local_index;
+  int expert_start;
+  int num_local;
+  const int32_t *expert_base;
+  int64_t capacity;  // < 0: unlimited
+  int64_t row_capacity;
+  int32_t *row_route;
+  int32_t *route_row;
+  int32_t *combine_rows;
+  int32_t *tile_expert;
+  int32_t *expert_offsets;
+  int32_t *expert_counts;
+  int32_t *mtiles;
+  int64_t max_mtiles;
+  int32_t *counters;
+  int64_t *stats;
+  const int32_t *hist;
+  int64_t chunk;
+  int nblk;
+};
+
+// Shared memory (int32 words): base[E1] tot[E1] run[E1] loc[E1]
+// warp_cnt[8][E1] lstart[L] lkept[L] gof[L] mstart[L] + 4 reduction words.
+__global__ void __launch_bounds__(kPackThreads) pack_scatter_kernel(ScatterArgs a) {
+  extern __shared__ int32_t sm[];
+  const int E = a.num_experts;
+  const int E1 = E + 1;
+  const int L = a.num_local;
+  int32_t *base = sm;
+  int32_t *tot = base + E1;
+  int32_t *run = tot + E1;
+  int32_t *loc = run + E1;
+  int32_t *warp_cnt = loc + E1;
+  int32_t *lstart = warp_cnt + kPackWarps * E1;
+  int32_t *lkept = lstart + L;
+  int32_t *gof = lkept + L;
+  int32_t *mstart = gof + L;
+  int32_t *red = mstart + L;  // [0] kept, [1] dropped, [2] total padded, [3] total mtiles
+
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int b = blockIdx.x;
+  const int64_t cap = a.capacity < 0 ? (int64_t)0x3fffffffffffffffLL : a.capacity;
+
+  for (int i = tid; i < L; i += blockDim.x) gof[i] = -1;
+  if (tid < 4) red[tid] = 0;
+  for (int i = tid; i < kPackWarps * E1; i += blockDim.x) warp_cnt[i] = 0;
+  __syncthreads();
+  for (int e = tid; e < E1; e += blockDim.x) {
+    int32_t before = 0, all = 0;
+    for (int bb = 0; bb < a.nblk; ++bb) {
+      const int32_t h = a.hist[static_cast<int64_t>(bb) * E1 + e];
+      if (bb < b) before += h;
+      all += h;
+    }
+    base[e] = before;
+    tot[e] = all;
+    run[e] = 0;
+    int l = -1;
+    if (e < E) {
+      if (a.local_index) {
+        const int64_t li = a.local_index[e];
+        if (li >= 0 && li < L) l = static_cast<int>(li);
+        else if (li >= L) atomicOr(&g_status, kStatusIndex);
+      } else if (e >= a.expert_start && e < a.expert_start + L) {
+        l = e - a.expert_start;
+      }
+    }
+    loc[e] = l;
+    if (l >= 0) gof[l] = e;
+  }
+  __syncthreads();
+
+  // Local layout: kept rows per local expert, 16-row padded starts, 128-row
+  // work-tile starts.  Warp 0 scans; each lane owns a contiguous range.
+  if (warp == 0) {
+    const int per = (L + 31) / 32;
+    const int l0 = min(L, lane * per);
+    const int l1 = min(L, l0 + per);
+    int64_t rows = 0, tiles = 0;
+    for (int l = l0; l < l1; ++l) {
+      const int g = gof[l];
+      int64_t kept = 0;
+      if (g >= 0) {
+        const int64_t eb = a.expert_base ? a.expert_base[g] : 0;
+        kept = min64(tot[g], max64(0, cap - eb));
+      }
+      lkept[l] = static_cast<int32_t>(kept);
+      rows += (kept + B200MOE_BLOCK_ROWS - 1) / B200MOE_BLOCK_ROWS * B200MOE_BLOCK_ROWS;
+      tiles += (kept + B200MOE_MTILE_ROWS - 1) / B200MOE_MTILE_ROWS;
+    }
+    int64_t rows_incl = rows, tiles_incl = tiles;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int64_t r = __shfl_up_sync(0xffffffffu, rows_incl, off);
+      const int64_t t = __shfl_up_sync(0xffffffffu, tiles_incl, off);
+      if (lane >= off) {
+        rows_incl += r;
+        tiles_incl += t;
+      }
+    }
+    int64_t row_off = rows_incl - rows, tile_off = tiles_incl - tiles;
+    for (int l = l0; l < l1; ++l) {
+      lstart[l] = static_cast<int32_t>(row_off);
+      mstart[l] = static_cast<int32_t>(tile_off);
+      const int64_t kept = lkept[l];
+      row_off += (kept + B200MOE_BLOCK_ROWS - 1) / B200MOE_BLOCK_ROWS * B200MOE_BLOCK_ROWS;
+      tile_off += (kept + B200MOE_MTILE_ROWS - 1) / B200MOE_MTILE_ROWS;
+    }
+    if (lane == 31) {
+      red[2] = static_cast<int32_t>(rows_incl);
+      red[3] = static_cast<int32_t>(tiles_incl);
+    }
+  }
+  __syncthreads();
+
+  if (b == 0) {
+    const int32_t total_rows = red[2];
+    int32_t total_tiles = red[3];
+    if (total_rows > a.row_capacity || total_tiles > a.max_mtiles) {
+      atomicOr(&g_status, kStatusIndex);
+      total_tiles = static_cast<int32_t>(min64(total_tiles, a.max_mtiles));
+    }
+    for (int l = tid; l < L; l += blockDim.x) {
+      a.expert_offsets[l] = lstart[l];
+      a.expert_counts[l] = lkept[l];
+      const int32_t kept = lkept[l];
+      const int32_t start = lstart[l];
+      const int32_t padded = (kept + B200MOE_BLOCK_ROWS - 1) / B200MOE_BLOCK_ROWS * B200MOE_BLOCK_ROWS;
+      for (int32_t t = start / B200MOE_BLOCK_ROWS; t < (start + padded) / B200MOE_BLOCK_ROWS; ++t)
+        if (t < a.row_capacity / B200MOE_BLOCK_ROWS) a.tile_expert[t] = l;
+      const int32_t nm = (kept + B200MOE_MTILE_ROWS - 1) / B200MOE_MTILE_ROWS;
+      for (int32_t i = 0; i < nm; ++i) {
+        const int64_t m = static_cast<int64_t>(mstart[l]) + i;
+        if (m >= a.max_mtiles) break;
+        a.mtiles[m * B200MOE_MTILE_WORDS + 0] = l;
+        a.mtiles[m * B200MOE_MTILE_WORDS + 1] = start + i * B200MOE_MTILE_ROWS;
+        a.mtiles[m * B200MOE_MTILE_WORDS + 2] = min(start + (i + 1) * B200MOE_MTILE_ROWS, start + kept);
+      }
+    }
+    if (tid == 0) {
+      a.expert_offsets[L] = total_rows;
+      a.counters[B200MOE_CNT_PADDED_ROWS] = total_rows;
+      a.counters[B200MOE_CNT_MTILES] = total_tiles;
+    }
+  }
+
+  // Rank this block's routes in order and scatter.
+  const int64_t begin = static_cast<int64_t>(b) * a.chunk;
+  const int64_t end = min(a.num_routes, begin + a.chunk);
+  int my_kept = 0, my_dropped = 0;
+  const int32_t route_sentinel = static_cast<int32_t>(a.num_routes);
+  const int32_t row_sentinel = static_cast<int32_t>(a.row_capacity);
+  for (int64_t sub = begin; sub < end; sub += kPackThreads) {
+    const int64_t r = sub + tid;
+    const bool active = r < end;
+    const int key = active ? route_key(a.ids[r], E) : -1 - lane;  // inactive lanes stay alone
+    const uint32_t peers = __match_any_sync(0xffffffffu, key);
+    const int rank = __popc(peers & lanemask_lt());
+    if (active && rank == 0) warp_cnt[warp * E1 + key] = __popc(peers);
+    __syncthreads();
+    int64_t pos = 0;
+    if (active) {
+      int32_t before = run[key];
+      for (int w = 0; w < warp; ++w) before += warp_cnt[w * E1 + key];
+      pos = static_cast<int64_t>(base[key]) + before + rank;
+    }
+    __syncthreads();
+    if (active && rank == 0) {
+      // Leaders of different warps may share a key.
+      atomicAdd(&run[key], __popc(peers));
+      warp_cnt[warp * E1 + key] = 0;
+    }
+    __syncwarp();
+    if (active) {
+      int32_t rr = row_sentinel, cr = route_sentinel;
+      if (key < E) {
+        const int64_t eb = a.expert_base ? a.expert_base[key] : 0;
+        if (eb + pos >= cap) {
+          a.ids[r] = E;
+          if (a.weights) a.weights[r] = __float2bfloat16_rn(0.f);
+          ++my_dropped;
+        } else {
+          const int l = loc[key];
+          if (l >= 0) {
+            const int64_t p = static_cast<int64_t>(lstart[l]) + pos;
+            if (p < a.row_capacity) {
+              a.row_route[p] = static_cast<int32_t>(r);
+              rr = static_cast<int32_t>(p);
+              cr = static_cast<int32_t>(r);
+              ++my_kept;
+            } else {
+              atomicOr(&g_status, kStatusIndex);
+            }
+          }
+        }
+      }
+      a.route_row[r] = rr;
+      if (a.combine_rows) a.combine_rows[r] = cr;
+    }
+  }
+  // Block totals -> global counters.
+  for (int off = 16; off > 0; off >>= 1) {
+    my_kept += __shfl_xor_sync(0xffffffffu, my_kept, off);
+    my_dropped += __shfl_xor_sync(0xffffffffu, my_dropped, off);
+  }
+  if (lane == 0) {
+    atomicAdd(&red[0], my_kept);
+    atomicAdd(&red[1], my_dropped);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    atomicAdd(&a.counters[B200MOE_CNT_LOCAL_KEPT], red[0]);
+    atomicAdd(&a.counters[B200MOE_CNT_DROPPED], red[1]);
+    if (a.stats) {
+      atomicAdd(reinterpret_cast<unsigned long long *>(&a.stats[0]),
+                static_cast<unsigned long long>(red[0]));
+      atomicAdd(reinterpret_cast<unsigned long long *>(&a.stats[1]),
+                static_cast<unsigned long long>(red[1]));
+    }
+  }
+}
+
+__global__ void histogram_kernel(const int64_t *__restrict__ ids, int64_t num_routes,
+                                 int num_experts, int32_t *__restrict__ counts) {
+  extern __shared__ int32_t sh[];
+  for (int e = threadIdx.x; e < num_experts; e += blockDim.x) sh[e] = 0;
+  __syncthreads();
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; r < num_routes;
+       r += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t e = ids[r];
+    if (e >= 0 && e < num_experts) atomicAdd(&sh[e], 1);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < num_experts; e += blockDim.x)
+    if (sh[e]) atomicAdd(&counts[e], sh[e]);
+}
+
+size_t scatter_smem_bytes(int num_experts, int num_local) {
+  const size_t E1 = static_cast<size_t>(num_experts) + 1;
+  return sizeof(int32_t) * (E1 * (4 + kPackWarps) + 4 * static_cast<size_t>(num_local) + 4);
+}
+
+}  // namespace
+}  // namespace b200moe
+
+extern "C" {
+
+int64_t b200moe_pack_row_capacity(int64_t num_routes, int num_local_experts) {
+  const int64_t active = num_routes < num_local_experts ? num_routes : num_local_experts;
+  const int64_t rows = num_routes + active * (B200MOE_BLOCK_ROWS - 1);
+  return (rows + B200MOE_BLOCK_ROWS - 1) / B200MOE_BLOCK_ROWS * B200MOE_BLOCK_ROWS;
+}
+
+int64_t b200moe_pack_max_mtiles(int64_t num_routes, int num_local_experts) {
+  const int64_t active = num_routes < num_local_experts ? num_routes : num_local_experts;
+  return (num_routes + B200MOE_MTILE_ROWS - 1) / B200MOE_MTILE_ROWS + active;
+}
+
+size_t b200moe_pack_scratch_bytes(int64_t num_routes, int num_experts) {
+  const auto g = b200moe::pack_geometry(num_routes);
+  return static_cast<size_t>(g.nblk) * (static_cast<size_t>(num_experts) + 1) * sizeof(int32_t);
+}
+
+int b200moe_pack_routes(int64_t *expert_ids, void *route_weights, int64_t num_routes,
+                        int num_experts, const int64_t *local_index, int expert_start,
+                        int num_local_experts, const int32_t *expert_base, int64_t capacity,
+                        int64_t row_capacity, int32_t *row_route, int32_t *route_row,
+                        int32_t *combine_rows, int32_t *tile_expert, int32_t *expert_offsets,
+                        int32_t *expert_counts, int32_t *mtiles, int64_t max_mtiles,
+                        int32_t *counters, int64_t *stats, void *scratch, size_t scratch_bytes,
+                        void *stream) {
+  using namespace b200moe;
+  B200_ARG(num_routes >= 0 && num_routes < (int64_t)0x7fffffff, "num_routes out of range");
+  B200_ARG(num_experts >= 1 && num_experts <= 4096, "num_experts must be in [1, 4096]");
+  B200_ARG(num_local_experts >= 1 && num_local_experts <= num_experts,
+           "num_local_experts must be in [1, num_experts]");
+  B200_ARG(counters != nullptr && expert_offsets && expert_counts, "null output pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (num_routes == 0) {
+    B200_CUDA(cudaMemsetAsync(counters, 0, sizeof(int32_t) * B200MOE_NUM_COUNTERS, s));
+    B200_CUDA(cudaMemsetAsync(expert_offsets, 0, sizeof(int32_t) * (num_local_experts + 1), s));
+    B200_CUDA(cudaMemsetAsync(expert_counts, 0, sizeof(int32_t) * num_local_experts, s));
+    return B200MOE_OK;
+  }
+  B200_ARG(expert_ids && row_route && route_row && tile_expert && mtiles, "null pointer argument");
+  B200_ARG(row_capacity >= b200moe_pack_row_capacity(num_routes, num_local_experts) &&
+               row_capacity % B200MOE_BLOCK_ROWS == 0 && row_capacity < (int64_t)0x7fffffff,
+           "row_capacity %lld too small or not a multiple of 16", (long long)row_capacity);
+  B200_ARG(max_mtiles >= b200moe_pack_max_mtiles(num_routes, num_local_experts),
+           "max_mtiles too small");
+  const auto g = pack_geometry(num_routes);
+  const size_t need = static_cast<size_t>(g.nblk) * (num_experts + 1) * sizeof(int32_t);
+  B200_ARG(scratch != nullptr && scratch_bytes >= need, "scratch needs %zu bytes", need);
+  int32_t *hist = static_cast<int32_t *>(scratch);
+
+  const size_t hist_smem = sizeof(int32_t) * (num_experts + 1);
+  pack_hist_kernel<<<g.nblk, kPackThreads, hist_smem, s>>>(
+      expert_ids, num_routes, num_experts, g.chunk, hist, row_route, row_capacity, tile_expert,
+      counters);
+  B200_LAUNCHED();
+
+  ScatterArgs a;
+  a.ids = expert_ids;
+  a.weights = static_cast<__nv_bfloat16 *>(route_weights);
+  a.num_routes = num_routes;
+  a.num_experts = num_experts;
+  a.local_index = local_index;
+  a.expert_start = expert_start;
+  a.num_local = num_local_experts;
+  a.expert_base = expert_base;
+  a.capacity = capacity;
+  a.row_capacity = row_capacity;
+  a.row_route = row_route;
+  a.route_row = route_row;
+  a.combine_rows = combine_rows;
+  a.tile_expert = tile_expert;
+  a.expert_offsets = expert_offsets;
+  a.expert_counts = expert_counts;
+  a.mtiles = mtiles;
+  a.max_mtiles = max_mtiles;
+  a.counters = counters;
+  a.stats = stats;
+  a.hist = hist;
+  a.chunk = g.chunk;
+  a.nblk = g.nblk;
+  const size_t smem = scatter_smem_bytes(num_experts, num_local_experts);
+  if (smem > 48 * 1024) {
+    B200_CUDA(cudaFuncSetAttribute(pack_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(smem)));
+  }
+  pack_scatter_kernel<<<g.nblk, kPackThreads, smem, s>>>(a);
+  B200_LAUNCHED();
+  return B200MOE_OK;
+}
+
+int b200moe_expert_histogram(const int64_t *expert_ids, int64_t num_routes, int num_experts,
+                             int32_t *counts, void *stream) {
+  using namespace b200moe;
+  B200_ARG(num_experts >= 1 && num_experts <= 4096, "num_experts must be in [1, 4096]");
+  B200_ARG(counts != nullptr, "counts must not be NULL");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  B200_CUDA(cudaMemsetAsync(counts, 0, sizeof(int32_t) * num_experts, s));
+  if (num_routes <= 0) return B200MOE_OK;
+  B200_ARG(expert_ids != nullptr, "expert_ids must not be NULL");
+  int64_t blocks = (num_routes + 1023) / 1024;
+  if (blocks > 4 * sm_count()) blocks = 4 * sm_count();
+  histogram_kernel<<<static_cast<int>(blocks), 256, sizeof(int32_t) * num_experts, s>>>(
+      expert_ids, num_routes, num_experts, counts);
+  B200_LAUNCHED();
+  return B200MOE_OK;
+}
+
+}  // extern "C"

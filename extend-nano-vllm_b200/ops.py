@@ -1,0 +1,229 @@
+"""Tensor-level wrappers of the b200moe C ABI.
+
+Every function enqueues its kernels on the current CUDA stream of the
+tensors' device and returns without synchronising.  Outputs are allocated
+through the PyTorch caching allocator, so the calls can be captured in CUDA
+graphs (no host synchronisation happens inside them).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from ._lib import call
+
+_DTYPE_CODES = {torch.bfloat16: _lib.BF16, torch.float16: _lib.F16,
+                torch.float32: _lib.F32, torch.float64: _lib.F64}
+
+
+def _p(t: torch.Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(t: torch.Tensor) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _require_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("b200moe kernels run on CUDA tensors only (no CPU path)")
+
+
+def _host_i32(values) -> ctypes.c_void_p:
+    """Host int32 array for the C ABI's *_host arguments (kept alive by the caller's frame)."""
+    arr = (ctypes.c_int32 * max(1, len(values)))(*[int(v) for v in values])
+    _host_i32.keep = arr  # the C call copies it into kernel arguments before returning
+    return ctypes.cast(arr, ctypes.c_void_p)
+
+
+def route_topk(logits: torch.Tensor, top_k: int, renormalize: bool
+               ) -> tuple[torch.Tensor, torch.Tensor]:
+    """fp32 softmax + top-k (+ renorm) of [T, E] logits -> (bf16 weights, int64 ids)."""
+    _require_cuda(logits)
+    logits = logits.contiguous()
+    if logits.dtype not in (torch.float32, torch.bfloat16, torch.float16):
+        raise TypeError(f"router logits must be fp32/bf16/fp16, got {logits.dtype}")
+    tokens, experts = logits.shape
+    weights = torch.empty((tokens, top_k), device=logits.device, dtype=torch.bfloat16)
+    ids = torch.empty((tokens, top_k), device=logits.device, dtype=torch.int64)
+    call("b200moe_route_topk", _p(logits), _DTYPE_CODES[logits.dtype], tokens, experts, top_k,
+         int(bool(renormalize)), _p(weights), _p(ids), _stream(logits))
+    return weights, ids
+
+
+@dataclass
+class PackedRoutes:
+    """Expert-major layout of a flat route array (see b200moe_pack_routes)."""
+
+    num_routes: int
+    row_capacity: int
+    max_mtiles: int
+    row_route: torch.Tensor      # [row_capacity] int32
+    route_row: torch.Tensor      # [num_routes] int32
+    combine_rows: torch.Tensor   # [num_routes] int32
+    tile_expert: torch.Tensor    # [row_capacity // 16] int32
+    expert_offsets: torch.Tensor  # [E_loc + 1] int32
+    expert_counts: torch.Tensor  # [E_loc] int32
+    mtiles: torch.Tensor         # [max_mtiles, 3] int32
+    counters: torch.Tensor       # [4] int32
+
+
+def pack_routes(expert_ids: torch.Tensor, route_weights: torch.Tensor | None,
+                num_experts: int, num_local_experts: int, *,
+                local_index: torch.Tensor | None = None, expert_start: int = 0,
+                expert_base: torch.Tensor | None = None, capacity: int | None = None,
+                stats: torch.Tensor | None = None) -> PackedRoutes:
+    """Capacity + expert-major packing of flat int64 routes.
+
+    With ``capacity`` set, dropped routes are rewritten in place in
+    ``expert_ids`` (to num_experts) and ``route_weights`` (to 0).
+    """
+    _require_cuda(expert_ids)
+    if expert_ids.dtype != torch.int64 or not expert_ids.is_contiguous():
+        raise TypeError("expert_ids must be a contiguous int64 tensor")
+    flat = expert_ids.view(-1)
+    routes = flat.numel()
+    device = flat.device
+    row_capacity = int(_lib.LIB.b200moe_pack_row_capacity(routes, num_local_experts))
+    max_mtiles = int(_lib.LIB.b200moe_pack_max_mtiles(routes, num_local_experts))
+    scratch_bytes = int(_lib.LIB.b200moe_pack_scratch_bytes(routes, num_experts))
+    i32 = dict(device=device, dtype=torch.int32)
+    row_route = torch.empty(row_capacity, **i32)
+    route_row = torch.empty(routes, **i32)
+    combine_rows = torch.empty(routes, **i32)
+    tile_expert = torch.empty(row_capacity // _lib.BLOCK_ROWS, **i32)
+    expert_offsets = torch.empty(num_local_experts + 1, **i32)
+    expert_counts = torch.empty(num_local_experts, **i32)
+    mtiles = torch.empty((max(1, max_mtiles), _lib.MTILE_WORDS), **i32)
+    counters = torch.empty(_lib.NUM_COUNTERS, **i32)
+    scratch = torch.empty(max(1, scratch_bytes // 4), **i32)
+    if local_index is not None:
+        if local_index.dtype != torch.int64 or local_index.numel() != num_experts:
+            raise TypeError("local_index must be int64 [num_experts]")
+    if expert_base is not None and expert_base.dtype != torch.int32:
+        raise TypeError("expert_base must be int32")
+    if route_weights is not None and (route_weights.dtype != torch.bfloat16
+                                      or route_weights.numel() != routes):
+        raise TypeError("route_weights must be bf16 with one weight per route")
+    call("b200moe_pack_routes", _p(flat), _p(route_weights), routes, num_experts,
+         _p(local_index), int(expert_start), num_local_experts, _p(expert_base),
+         -1 if capacity is None else int(capacity), row_capacity, _p(row_route),
+         _p(route_row), _p(combine_rows), _p(tile_expert), _p(expert_offsets),
+         _p(expert_counts), _p(mtiles), max_mtiles, _p(counters), _p(stats), _p(scratch),
+         scratch.numel() * 4, _stream(flat))
+    return PackedRoutes(routes, row_capacity, max_mtiles, row_route, route_row, combine_rows,
+                        tile_expert, expert_offsets, expert_counts, mtiles, counters)
+
+
+def expert_histogram(expert_ids: torch.Tensor, num_experts: int) -> torch.Tensor:
+    _require_cuda(expert_ids)
+    flat = expert_ids.reshape(-1).contiguous()
+    counts = torch.empty(num_experts, device=flat.device, dtype=torch.int32)
+    call("b200moe_expert_histogram", _p(flat), flat.numel(), num_experts, _p(counts),
+         _stream(flat))
+    return counts
+
+
+def gather_rows(x: torch.Tensor, packed: PackedRoutes, top_k: int,
+                token_of_route: torch.Tensor | None = None) -> torch.Tensor:
+    hidden = x.size(1)
+    x_packed = torch.empty((packed.row_capacity, hidden), device=x.device, dtype=x.dtype)
+    call("b200moe_gather_rows", _p(x), x.size(0), hidden, _p(packed.row_route),
+         _p(token_of_route), top_k, packed.num_routes, packed.row_capacity,
+         _p(packed.counters), _p(x_packed), _stream(x))
+    return x_packed
+
+
+def expert_gate_up(engine: int, x: torch.Tensor, x_packed: torch.Tensor | None,
+                   w13: torch.Tensor, packed: PackedRoutes, top_k: int,
+                   token_of_route: torch.Tensor | None = None) -> torch.Tensor:
+    """SwiGLU(x W13^T) per packed row -> act [row_capacity, I] (packed order)."""
+    num_local, two_inter, hidden = w13.shape
+    inter = two_inter // 2
+    act = torch.empty((packed.row_capacity, inter), device=x.device, dtype=torch.bfloat16)
+    call("b200moe_expert_gate_up", engine, _p(x), x.size(0), _p(x_packed), hidden, inter,
+         _p(w13), num_local, _p(packed.row_route), _p(token_of_route), top_k,
+         packed.num_routes, packed.row_capacity, _p(packed.mtiles), packed.max_mtiles,
+         _p(packed.counters), _p(act), _stream(x))
+    return act
+
+
+def expert_down(engine: int, act: torch.Tensor, w2: torch.Tensor, packed: PackedRoutes,
+                route_weights: torch.Tensor) -> torch.Tensor:
+    """Route-weighted down projection -> y [num_routes, H] in route order.
+
+    Rows of routes that are not computed here are left unwritten; combine masks
+    them through ``packed.combine_rows``.
+    """
+    num_local, hidden, inter = w2.shape
+    y = torch.empty((packed.num_routes, hidden), device=act.device, dtype=torch.bfloat16)
+    call("b200moe_expert_down", engine, _p(act), hidden, inter, _p(w2), num_local,
+         _p(packed.row_route), _p(route_weights), packed.num_routes, packed.row_capacity,
+         _p(packed.mtiles), packed.max_mtiles, _p(packed.counters), _p(y), _stream(act))
+    return y
+
+
+def combine(y: torch.Tensor, route_rows: torch.Tensor | None, num_tokens: int, top_k: int,
+            out_dtype: torch.dtype = torch.bfloat16, accum_f64: bool = False) -> torch.Tensor:
+    """out[t] = sum_s y[route_rows[t*k+s]] in slot order (rows >= len(y) are zero)."""
+    _require_cuda(y)
+    if y.dtype != torch.bfloat16:
+        raise TypeError("combine input must be bf16")
+    y = y.contiguous()
+    hidden = y.size(1)
+    out = torch.empty((num_tokens, hidden), device=y.device, dtype=out_dtype)
+    if route_rows is not None:
+        route_rows = route_rows.to(torch.int32).contiguous()
+    call("b200moe_combine", _p(y), y.size(0), _p(route_rows), num_tokens, top_k, hidden,
+         int(bool(accum_f64)), _p(out), _DTYPE_CODES[out_dtype], _stream(y))
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Expert-parallel exchange helpers.
+# ---------------------------------------------------------------------------
+def ep_plan(expert_ids: torch.Tensor, owner: torch.Tensor, ep_size: int, num_experts: int):
+    tokens, top_k = expert_ids.shape
+    device = expert_ids.device
+    send_token_slot = torch.empty((tokens, ep_size), device=device, dtype=torch.int32)
+    route_dest_slot = torch.empty(tokens * top_k, device=device, dtype=torch.int32)
+    counts = torch.empty(2 * ep_size, device=device, dtype=torch.int32)
+    call("b200moe_ep_plan", _p(expert_ids), tokens, top_k, num_experts, _p(owner), ep_size,
+         _p(send_token_slot), _p(route_dest_slot), _p(counts), _stream(expert_ids))
+    return send_token_slot, route_dest_slot, counts
+
+
+def ep_pack(x, expert_ids, route_weights, owner, ep_size, num_experts, send_token_slot,
+            route_dest_slot, token_offsets, route_offsets, send_x, send_meta) -> None:
+    tokens, top_k = expert_ids.shape
+    call("b200moe_ep_pack", _p(x), x.size(1), _p(expert_ids), _p(route_weights), tokens, top_k,
+         num_experts, _p(owner), ep_size, _p(send_token_slot), _p(route_dest_slot),
+         _host_i32(token_offsets), _host_i32(route_offsets), _p(send_x), _p(send_meta),
+         _stream(x))
+
+
+def ep_unpack_routes(recv_meta, ep_size, recv_route_offsets, recv_token_offsets):
+    n = recv_meta.size(0)
+    device = recv_meta.device
+    ids = torch.empty(n, device=device, dtype=torch.int64)
+    token_of_route = torch.empty(n, device=device, dtype=torch.int32)
+    weights = torch.empty(n, device=device, dtype=torch.bfloat16)
+    call("b200moe_ep_unpack_routes", _p(recv_meta), n, ep_size, _host_i32(recv_route_offsets),
+         _host_i32(recv_token_offsets), _p(ids), _p(token_of_route), _p(weights),
+         _stream(recv_meta))
+    return ids, token_of_route, weights
+
+
+def ep_return_rows(expert_ids, owner, ep_size, num_experts, route_dest_slot, route_offsets,
+                   num_rows_returned) -> torch.Tensor:
+    flat = expert_ids.reshape(-1)
+    rows = torch.empty(flat.numel(), device=flat.device, dtype=torch.int32)
+    call("b200moe_ep_return_rows", _p(flat), _p(owner), flat.numel(), num_experts, ep_size,
+         _p(route_dest_slot), _host_i32(route_offsets), int(num_rows_returned), _p(rows),
+         _stream(flat))
+    return rows

@@ -1,0 +1,264 @@
+/*
+ * b200moe.h -- C ABI of the B200 (sm_100a) Qwen3-MoE expert-execution path.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * passed as `void *`.  Nothing here allocates device memory: the caller owns
+ * every buffer (the Python host layer allocates them through the PyTorch
+ * caching allocator so the calls can be captured in CUDA graphs).  Work is
+ * enqueued on `stream` and the call returns without synchronising.
+ *
+ * Return value: B200MOE_OK (0) or an error code; b200moe_last_error() gives a
+ * thread-local message for the last failing call on the calling thread.
+ *
+ * Reference interfaces are cited as file:line inside kagami4243/extend-nano-vLLM
+ * (package `nanovllm`, version 0.3.0).  The reference implements this path in
+ * Python + Triton inside class ExpertParallelMoE (nanovllm/layers/moe.py:237);
+ * these functions replace its router, packing, grouped GEMM, SwiGLU, combine
+ * and expert-parallel exchange steps.
+ */
+#ifndef B200MOE_H_
+#define B200MOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define B200MOE_API __attribute__((visibility("default")))
+#else
+#define B200MOE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define B200MOE_OK 0
+#define B200MOE_EINVAL 1      /* bad argument (shape, dtype, null pointer) */
+#define B200MOE_ECUDA 2       /* CUDA runtime / driver error */
+#define B200MOE_EUNSUPPORTED 3 /* valid but unsupported configuration */
+
+/* ---- element type codes -------------------------------------------------- */
+#define B200MOE_BF16 0
+#define B200MOE_F16 1
+#define B200MOE_F32 2
+#define B200MOE_F64 3
+
+/* ---- expert GEMM engines ---------------------------------------------------- */
+#define B200MOE_ENGINE_STREAM 0 /* CUDA-core weight streaming (small decode buckets) */
+#define B200MOE_ENGINE_TCGEN05 1 /* tcgen05/TMEM grouped GEMM fed by TMA */
+
+/* Size of the 128-row work-tile records written by b200moe_pack_routes:
+ * {local expert, first packed row, end packed row (exclusive)}. */
+#define B200MOE_MTILE_WORDS 3
+#define B200MOE_MTILE_ROWS 128
+/* Packing alignment of every expert's row group (reference _MOE_BLOCK_M,
+ * nanovllm/layers/moe.py:36). */
+#define B200MOE_BLOCK_ROWS 16
+
+/* counters[] written by b200moe_pack_routes */
+#define B200MOE_CNT_PADDED_ROWS 0 /* reference num_tokens_post_padded, moe.py:807 */
+#define B200MOE_CNT_MTILES 1      /* number of 128-row work tiles */
+#define B200MOE_CNT_LOCAL_KEPT 2  /* local assignments, moe.py:864-867 */
+#define B200MOE_CNT_DROPPED 3     /* capacity drops, moe.py:913-917 */
+#define B200MOE_NUM_COUNTERS 4
+
+B200MOE_API const char *b200moe_last_error(void);
+B200MOE_API int b200moe_abi_version(void);
+
+/* Sticky device-side status word: non-zero after a kernel gave up a bounded
+ * wait (bit 0) or saw an out-of-range index (bit 1).  Copies the word of the
+ * current device to *status (synchronises) and, if clear != 0, resets it. */
+B200MOE_API int b200moe_device_status(int *status, int clear);
+
+/*
+ * Router: softmax (fp32) over `num_experts` logits per token, top-k selection,
+ * optional renormalisation over the selected k, bf16 weights.
+ * Replaces ExpertParallelMoE._route softmax/topk/renorm/cast,
+ * nanovllm/layers/moe.py:872-878 (the gate projection moe.py:871 stays a
+ * library GEMM in the caller).
+ * Ranking: descending logit, ties broken by the lower expert index.  Softmax
+ * is monotone, so this is the reference's top-k of probabilities with a
+ * defined tie order.
+ *   logits     [num_tokens, num_experts] of logits_dtype (BF16/F16/F32), row-major
+ *   weights    [num_tokens, top_k] bf16 out
+ *   expert_ids [num_tokens, top_k] int64 out
+ * Limits: num_experts <= 1024, top_k <= min(32, num_experts).
+ */
+B200MOE_API int b200moe_route_topk(const void *logits, int logits_dtype, int64_t num_tokens,
+                       int num_experts, int top_k, int renormalize,
+                       void *weights, int64_t *expert_ids, void *stream);
+
+/* Scratch bytes b200moe_pack_routes needs for `num_routes` routes. */
+B200MOE_API size_t b200moe_pack_scratch_bytes(int64_t num_routes, int num_experts);
+
+/* Rows the packed layout can occupy: num_routes + min(num_routes, E_loc) * 15,
+ * rounded up to 16 (reference max_padded_rows, moe.py:793-797). */
+B200MOE_API int64_t b200moe_pack_row_capacity(int64_t num_routes, int num_local_experts);
+
+/* Upper bound of 128-row work tiles: ceil(num_routes/128) + min(num_routes, E_loc). */
+B200MOE_API int64_t b200moe_pack_max_mtiles(int64_t num_routes, int num_local_experts);
+
+/*
+ * Capacity + expert-major packing, graph-safe (no host synchronisation).
+ * Replaces: capacity keep-mask, moe.py:879-919; _local_routes and the Triton
+ * _map_expert_routes_kernel, moe.py:491-517 and :142-161; compact expert-task
+ * construction of _forward_static_decode, moe.py:790-847; the dynamic packing
+ * of _forward_triton, moe.py:698-740 and :763-767.
+ *
+ * Routes are the flat [num_routes] array `expert_ids` in token-major, slot-
+ * minor order.  A route's capacity position is expert_base[e] (0 when NULL)
+ * plus the number of earlier routes to the same expert; it is kept when the
+ * position is < capacity (capacity < 0: no limit).  Dropped routes are
+ * rewritten in place to id = num_experts and weight 0 (moe.py:918-919).
+ * Local experts are [expert_start, expert_start + num_local_experts) when
+ * local_index is NULL, else local_index[e] (>= 0 local id, -1 remote).
+ * Ids outside [0, num_experts) are never local (moe.py:512-517).
+ *
+ * Outputs (all int32, caller-allocated):
+ *   row_route      [row_capacity]   packed row -> route id, unused rows = num_routes
+ *                                   (reference row_ids in route layout, moe.py:828-832)
+ *   route_row      [num_routes]     route -> packed row, else row_capacity
+ *                                   (reference route_rows, moe.py:763-767)
+ *   combine_rows   [num_routes]     route -> route id if computed here, else num_routes
+ *                                   (may be NULL)
+ *   tile_expert    [row_capacity/16] local expert of each 16-row tile, unused 0
+ *                                   (reference expert_ids, moe.py:833-844)
+ *   expert_offsets [E_loc + 1]      first packed row of each local expert; [E_loc] = total
+ *   expert_counts  [E_loc]          kept local routes per expert
+ *   mtiles         [max_mtiles * 3] 128-row work tiles {expert, row_begin, row_end}
+ *   counters       [4]              see B200MOE_CNT_*
+ *   stats          [2] int64 or NULL: += local kept, += dropped (device accumulators)
+ */
+B200MOE_API int b200moe_pack_routes(int64_t *expert_ids, void *route_weights, int64_t num_routes,
+                        int num_experts, const int64_t *local_index, int expert_start,
+                        int num_local_experts, const int32_t *expert_base,
+                        int64_t capacity, int64_t row_capacity, int32_t *row_route,
+                        int32_t *route_row, int32_t *combine_rows, int32_t *tile_expert,
+                        int32_t *expert_offsets, int32_t *expert_counts, int32_t *mtiles,
+                        int64_t max_mtiles, int32_t *counters, int64_t *stats,
+                        void *scratch, size_t scratch_bytes, void *stream);
+
+/*
+ * Per-expert route counts of a flat route array: counts[e] for e < num_experts
+ * (ids outside the range are ignored).  Used by the expert-parallel exchange to
+ * agree on global capacity positions (the reference routes the gathered global
+ * batch, moe.py:979).
+ */
+B200MOE_API int b200moe_expert_histogram(const int64_t *expert_ids, int64_t num_routes, int num_experts,
+                             int32_t *counts, void *stream);
+
+/*
+ * Gather the hidden rows of packed routes into expert-major order:
+ * x_packed[p] = x[token(row_route[p])] for p < counters[PADDED_ROWS] and
+ * row_route[p] < num_routes, where token(r) = token_of_route[r] when given,
+ * else r / top_k.  Feeds the tcgen05 gate/up GEMM (reference A-row gather of
+ * _grouped_moe_gemm_kernel, moe.py:103-118).
+ */
+B200MOE_API int b200moe_gather_rows(const void *x, int64_t x_rows, int hidden, const int32_t *row_route,
+                        const int32_t *token_of_route, int top_k, int64_t num_routes,
+                        int64_t row_capacity, const int32_t *counters, void *x_packed,
+                        void *stream);
+
+/*
+ * Grouped gate/up projection fused with SwiGLU:
+ *   act[p, j] = bf16( bf16(silu(bf16(g))) * bf16(u) ),  g = x_p . W13[e, j],
+ *   u = x_p . W13[e, I + j], fp32 accumulation, for every packed row p of
+ *   local expert e.  Rounding points follow the reference, which stores
+ *   gate/up in bf16 and applies F.silu and the product in bf16
+ *   (moe.py:848-854 and :742-746, kernel moe.py:63-139).
+ *   w13   [E_loc, 2I, H] bf16 (gate rows first, moe.py:532-539)
+ *   act   [row_capacity, I] bf16 out, packed order
+ * engine STREAM reads x ([x_rows, H], token-major) through row_route;
+ * engine TCGEN05 reads x_packed ([row_capacity, H], from b200moe_gather_rows).
+ */
+B200MOE_API int b200moe_expert_gate_up(int engine, const void *x, int64_t x_rows, const void *x_packed,
+                           int hidden, int inter, const void *w13, int num_local_experts,
+                           const int32_t *row_route, const int32_t *token_of_route, int top_k,
+                           int64_t num_routes, int64_t row_capacity, const int32_t *mtiles,
+                           int64_t max_mtiles, const int32_t *counters, void *act, void *stream);
+
+/*
+ * Grouped down projection with the route-weight scale applied to the fp32
+ * accumulator before the bf16 store (moe.py:129-139; pinned by the reference
+ * xfail test tests/test_moe_graph_capture.py:151-174):
+ *   y[r, h] = bf16( (act_p . W2[e, h]) * float(w_r) ),  r = row_route[p]
+ *   w2  [E_loc, H, I] bf16;  route_weights [num_routes] bf16;
+ *   y   [num_routes, H] bf16 out in route order (rows of routes not computed
+ *       here are not written; combine masks them through combine_rows).
+ */
+B200MOE_API int b200moe_expert_down(int engine, const void *act, int hidden, int inter, const void *w2,
+                        int num_local_experts, const int32_t *row_route,
+                        const void *route_weights, int64_t num_routes, int64_t row_capacity,
+                        const int32_t *mtiles, int64_t max_mtiles, const int32_t *counters,
+                        void *y, void *stream);
+
+/*
+ * Route-order combine: out[t, :] = sum_{s < top_k} Y[route_rows[t*top_k+s], :]
+ * accumulated in fp32 (accum_f64 != 0: fp64) in slot order, rows >= num_rows
+ * read as zero, stored as out_dtype (BF16/F32/F64).  route_rows NULL means the
+ * identity.  Replaces _combine_expert_routes and the Triton
+ * _combine_expert_routes_kernel, moe.py:642-678 and :164-192.
+ */
+B200MOE_API int b200moe_combine(const void *y, int64_t num_rows, const int32_t *route_rows,
+                    int64_t num_tokens, int top_k, int hidden, int accum_f64, void *out,
+                    int out_dtype, void *stream);
+
+/*
+ * Expert-parallel dispatch plan for the NCCL all-to-all backend
+ * "all_to_all_nvlink" (replaces the token all-gather and global re-routing of
+ * _forward_global_dp, nanovllm/layers/moe.py:964-982).  For this rank's flat
+ * routes (after capacity) and owner[e], the EP rank that holds expert e:
+ *   send_token_slot [num_tokens * ep_size]  slot of token t in destination d's
+ *                    token list, or -1 (t has no kept route to d)
+ *   route_dest_slot [num_tokens * top_k]    slot of route r in its destination's
+ *                    route list, or -1 (dropped / invalid id)
+ *   counts [2 * ep_size] int32: tokens per destination, then routes per destination
+ * Lists are in ascending token / route order.  ep_size <= 16.
+ */
+B200MOE_API int b200moe_ep_plan(const int64_t *expert_ids, int64_t num_tokens, int top_k, int num_experts,
+                    const int32_t *owner, int ep_size, int32_t *send_token_slot,
+                    int32_t *route_dest_slot, int32_t *counts, void *stream);
+
+/*
+ * Pack the dispatch payload.  token_offsets_host / route_offsets_host are HOST
+ * arrays [ep_size]: exclusive prefix sums of the plan counts.
+ *   send_x     [sum tokens, H] bf16 rows, grouped by destination
+ *   send_meta  [sum routes, 4] int32 records {global expert id, token row in the
+ *              destination's token list, bf16 weight bits, source route id}
+ */
+B200MOE_API int b200moe_ep_pack(const void *x, int hidden, const int64_t *expert_ids,
+                    const void *route_weights, int64_t num_tokens, int top_k, int num_experts,
+                    const int32_t *owner, int ep_size, const int32_t *send_token_slot,
+                    const int32_t *route_dest_slot, const int32_t *token_offsets_host,
+                    const int32_t *route_offsets_host, void *send_x, int32_t *send_meta,
+                    void *stream);
+
+/*
+ * Receiver: expand received route records into the flat arrays the local
+ * pipeline consumes.  recv_route_offsets_host [ep_size + 1] and
+ * recv_token_offsets_host [ep_size] are HOST prefix sums of what each source
+ * sent.  Outputs: expert_ids (global ids), token_of_route (row in the received
+ * token buffer), route_weights (bf16).
+ */
+B200MOE_API int b200moe_ep_unpack_routes(const int32_t *recv_meta, int64_t num_recv_routes, int ep_size,
+                             const int32_t *recv_route_offsets_host,
+                             const int32_t *recv_token_offsets_host, int64_t *expert_ids,
+                             int32_t *token_of_route, void *route_weights, void *stream);
+
+/*
+ * Source, after the return all-to-all: route r's result is row
+ * route_offsets_host[dest(r)] + route_dest_slot[r] of the returned buffer;
+ * combine_rows[r] gets that row or num_rows_returned (dropped routes).  The
+ * combine then runs in slot order as with EP=1 (moe.py:642-678).
+ */
+B200MOE_API int b200moe_ep_return_rows(const int64_t *expert_ids, const int32_t *owner, int64_t num_routes,
+                           int num_experts, int ep_size, const int32_t *route_dest_slot,
+                           const int32_t *route_offsets_host, int64_t num_rows_returned,
+                           int32_t *combine_rows, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200MOE_H_ */

@@ -1,0 +1,299 @@
+"""CPU oracle of the Qwen3-MoE expert path -- TEST INFRASTRUCTURE ONLY.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline
+leg may import this module; the product path never does.
+
+It restates, in numpy (integer/routing work) and torch-CPU fp32 (expert
+math), the algorithm of ``nanovllm.layers.moe.ExpertParallelMoE`` from
+kagami4243/extend-nano-vLLM 0.3.0.  Each function cites the reference lines
+it follows.  Parity pinning: ``tests/test_oracle_golden.py`` checks these
+functions against golden vectors produced by the reference itself
+(``tests/golden/make_golden.py`` imports the reference on CPU and records
+its outputs).
+
+Conventions shared with the CUDA library:
+  * top-k ranks by descending logit, ties to the lower expert index (softmax
+    is monotone; the reference's torch.topk leaves tie order unspecified);
+  * rounding points of the reference's GPU path (moe.py:742-746, :848-858):
+    gate/up stored in bf16, silu and the product rounded to bf16, the route
+    weight applied to the fp32 down accumulator before the bf16 store, the
+    combine summed in fp32 in slot order (moe.py:164-192).
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+
+BLOCK_ROWS = 16      # reference _MOE_BLOCK_M, moe.py:36
+MTILE_ROWS = 128     # work-tile rows of the CUDA library
+
+
+# ---------------------------------------------------------------------------
+# bf16 helpers
+# ---------------------------------------------------------------------------
+def bf16_round(a) -> np.ndarray:
+    """Round float32 values to the nearest bf16 (ties to even), as float32."""
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    u = a.view(np.uint32).astype(np.uint64)
+    rounded = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16
+    out = rounded.astype(np.uint32).view(np.float32)
+    return np.where(np.isnan(a), a, out)
+
+
+def bf16_bits(a) -> np.ndarray:
+    return (bf16_round(a).view(np.uint32) >> 16).astype(np.uint16)
+
+
+def from_bf16_bits(bits) -> np.ndarray:
+    return (np.asarray(bits, dtype=np.uint32) << 16).view(np.float32)
+
+
+# ---------------------------------------------------------------------------
+# Router (moe.py:870-878)
+# ---------------------------------------------------------------------------
+def softmax_f32(logits: np.ndarray) -> np.ndarray:
+    logits = np.asarray(logits, dtype=np.float32)
+    m = logits.max(axis=-1, keepdims=True)
+    e = np.exp(logits - m, dtype=np.float32)
+    return (e / e.sum(axis=-1, keepdims=True, dtype=np.float32)).astype(np.float32)
+
+
+def route_topk(logits: np.ndarray, top_k: int, renormalize: bool
+               ) -> tuple[np.ndarray, np.ndarray]:
+    """softmax(fp32) -> top-k -> optional renorm -> bf16 (moe.py:871-878).
+
+    Returns (weights as bf16-rounded float32 [T, k], ids int64 [T, k]).
+    """
+    logits = np.asarray(logits, dtype=np.float32)
+    probs = softmax_f32(logits)
+    # Stable argsort of -logit: descending value, ascending index on ties.
+    order = np.argsort(-logits, axis=-1, kind="stable")[:, :top_k]
+    ids = order.astype(np.int64)
+    w = np.take_along_axis(probs, order, axis=-1).astype(np.float32)
+    if renormalize:
+        total = np.zeros(w.shape[0], dtype=np.float32)
+        for s in range(top_k):  # sequential fp32 sum over the slots
+            total = (total + w[:, s]).astype(np.float32)
+        w = (w / total[:, None]).astype(np.float32)
+    return bf16_round(w), ids
+
+
+def tie_tokens(logits: np.ndarray, top_k: int) -> np.ndarray:
+    """Tokens whose top-(k+1) logits contain a tie (order there is unspecified
+    in the reference)."""
+    logits = np.asarray(logits, dtype=np.float32)
+    top = -np.sort(-logits, axis=-1)[:, : top_k + 1]
+    return np.any(top[:, 1:] == top[:, :-1], axis=-1)
+
+
+# ---------------------------------------------------------------------------
+# Capacity (moe.py:879-919)
+# ---------------------------------------------------------------------------
+def capacity_of(num_tokens: int, top_k: int, num_experts: int,
+                expert_capacity: int | None, capacity_factor: float | None) -> int | None:
+    """moe.py:880-886, same float expression order."""
+    if expert_capacity is not None:
+        return int(expert_capacity)
+    if capacity_factor is not None:
+        return max(1, math.ceil(capacity_factor * num_tokens * top_k / num_experts))
+    return None
+
+
+def expert_positions(flat_ids: np.ndarray, num_experts: int) -> np.ndarray:
+    """Position of each route among earlier routes to the same expert (stable
+    argsort + group offsets, moe.py:887-909).  Invalid ids get their own key."""
+    flat = np.asarray(flat_ids, dtype=np.int64).reshape(-1)
+    keys = np.where((flat >= 0) & (flat < num_experts), flat, num_experts)
+    order = np.argsort(keys, kind="stable")
+    sorted_keys = keys[order]
+    idx = np.arange(flat.size)
+    start = np.ones(flat.size, dtype=bool)
+    start[1:] = sorted_keys[1:] != sorted_keys[:-1]
+    first = np.maximum.accumulate(np.where(start, idx, 0)) if flat.size else idx
+    pos = np.empty(flat.size, dtype=np.int64)
+    pos[order] = idx - first
+    return pos
+
+
+def apply_capacity(weights: np.ndarray, ids: np.ndarray, num_experts: int,
+                   capacity: int | None, expert_base: np.ndarray | None = None):
+    """keep = base[e] + position < capacity; dropped -> weight 0, id E
+    (moe.py:910-919).  Returns (weights, ids, keep) as new arrays."""
+    ids = np.array(ids, dtype=np.int64, copy=True)
+    weights = np.array(weights, dtype=np.float32, copy=True)
+    if capacity is None:
+        return weights, ids, np.ones(ids.shape, dtype=bool)
+    flat = ids.reshape(-1)
+    pos = expert_positions(flat, num_experts)
+    valid = (flat >= 0) & (flat < num_experts)
+    base = np.zeros(flat.size, dtype=np.int64)
+    if expert_base is not None:
+        base[valid] = np.asarray(expert_base, dtype=np.int64)[flat[valid]]
+    keep = ~valid | (base + pos < capacity)
+    keep = keep.reshape(ids.shape)
+    dropped = valid.reshape(ids.shape) & ~keep
+    weights[dropped] = 0.0
+    ids[dropped] = num_experts
+    return weights, ids, ~dropped
+
+
+# ---------------------------------------------------------------------------
+# Local-route mapping and packing (moe.py:491-517, :698-740, :783-847)
+# ---------------------------------------------------------------------------
+def local_ids(flat_ids: np.ndarray, num_experts: int, num_local: int,
+              expert_start: int = 0, local_index: np.ndarray | None = None) -> np.ndarray:
+    """Local expert id of each route or -1 (moe.py:494-517)."""
+    flat = np.asarray(flat_ids, dtype=np.int64).reshape(-1)
+    valid = (flat >= 0) & (flat < num_experts)
+    if local_index is None:
+        local = flat - expert_start
+        ok = valid & (local >= 0) & (local < num_local)
+    else:
+        li = np.asarray(local_index, dtype=np.int64)
+        local = np.where(valid, li[np.clip(flat, 0, num_experts - 1)], -1)
+        ok = valid & (local >= 0)
+    return np.where(ok, local, -1)
+
+
+def row_capacity(num_routes: int, num_local: int) -> int:
+    """moe.py:793-797."""
+    active = min(num_routes, num_local)
+    rows = num_routes + active * (BLOCK_ROWS - 1)
+    return (rows + BLOCK_ROWS - 1) // BLOCK_ROWS * BLOCK_ROWS
+
+
+def pack(flat_ids: np.ndarray, num_experts: int, num_local: int, expert_start: int = 0,
+         local_index: np.ndarray | None = None) -> dict:
+    """Expert-major 16-aligned layout of the local routes.
+
+    Keys: row_route (reference static row_ids with sentinel = num_routes,
+    moe.py:828-846), tile_expert (reference expert_ids, :833-844),
+    padded_rows (num_tokens_post_padded, :807), route_row (dynamic-path
+    route_rows with sentinel = row_capacity, :763-767), expert_offsets,
+    expert_counts, combine_rows (route id if local else num_routes), mtiles
+    (128-row work tiles of the CUDA library).
+    """
+    flat = np.asarray(flat_ids, dtype=np.int64).reshape(-1)
+    R = flat.size
+    cap_rows = row_capacity(R, num_local)
+    local = local_ids(flat, num_experts, num_local, expert_start, local_index)
+    counts = np.bincount(local[local >= 0], minlength=num_local).astype(np.int64)
+    padded = (counts + BLOCK_ROWS - 1) // BLOCK_ROWS * BLOCK_ROWS
+    starts = np.cumsum(padded) - padded
+    total = int(padded.sum())
+    row_route = np.full(cap_rows, R, dtype=np.int64)
+    route_row = np.full(R, cap_rows, dtype=np.int64)
+    combine_rows = np.full(R, R, dtype=np.int64)
+    # Stable expert-major order of local routes (moe.py:808-832).
+    sel = np.nonzero(local >= 0)[0]
+    order = sel[np.argsort(local[sel], kind="stable")]
+    within = np.arange(order.size) - (np.cumsum(counts) - counts)[local[order]]
+    positions = starts[local[order]] + within
+    row_route[positions] = order
+    route_row[order] = positions
+    combine_rows[order] = order
+    tile_expert = np.zeros(cap_rows // BLOCK_ROWS, dtype=np.int64)
+    for e in range(num_local):
+        tile_expert[starts[e] // BLOCK_ROWS:(starts[e] + padded[e]) // BLOCK_ROWS] = e
+    mtiles = []
+    for e in range(num_local):
+        for i in range(0, int(counts[e]), MTILE_ROWS):
+            mtiles.append((e, int(starts[e] + i), int(starts[e] + min(counts[e], i + MTILE_ROWS))))
+    return dict(row_route=row_route, tile_expert=tile_expert, padded_rows=total,
+                route_row=route_row, combine_rows=combine_rows,
+                expert_offsets=np.append(starts, total), expert_counts=counts,
+                mtiles=np.array(mtiles, dtype=np.int64).reshape(-1, 3),
+                local_kept=int(counts.sum()))
+
+
+# ---------------------------------------------------------------------------
+# Expert math (Triton path numerics, moe.py:63-139, :742-770, :848-863)
+# ---------------------------------------------------------------------------
+def _t32(a) -> torch.Tensor:
+    return torch.as_tensor(np.asarray(a, dtype=np.float32))
+
+
+def expert_rows(x: np.ndarray, w13: np.ndarray, w2: np.ndarray, flat_ids: np.ndarray,
+                flat_weights: np.ndarray, tokens_of_route: np.ndarray, num_experts: int,
+                num_local: int, expert_start: int = 0,
+                local_index: np.ndarray | None = None) -> tuple[np.ndarray, np.ndarray]:
+    """Per-route expert output y [R, H] (bf16-valued float32) and a mask of the
+    routes computed here.  x, w13, w2, flat_weights hold bf16 values."""
+    flat = np.asarray(flat_ids, dtype=np.int64).reshape(-1)
+    local = local_ids(flat, num_experts, num_local, expert_start, local_index)
+    H = x.shape[1]
+    inter = w13.shape[1] // 2
+    y = np.zeros((flat.size, H), dtype=np.float32)
+    xt = _t32(x)
+    for e in np.unique(local[local >= 0]):
+        routes = np.nonzero(local == e)[0]
+        a = xt[torch.as_tensor(tokens_of_route[routes])]
+        gu = a @ _t32(w13[e]).T                       # fp32 accumulate
+        g = bf16_round(gu[:, :inter].numpy())
+        u = bf16_round(gu[:, inter:].numpy())
+        s = bf16_round(g / (1.0 + np.exp(-g, dtype=np.float32)))
+        act = bf16_round(s * u)
+        d = (_t32(act) @ _t32(w2[e]).T).numpy()       # fp32 accumulate
+        w = np.asarray(flat_weights, dtype=np.float32)[routes][:, None]
+        y[routes] = bf16_round(d * w)
+    return y, local >= 0
+
+
+def combine(y: np.ndarray, route_rows: np.ndarray, num_tokens: int, top_k: int,
+            accum=np.float32) -> np.ndarray:
+    """out[t] = sum_s Y[route_rows[t*k+s]] in slot order, rows >= len(Y) are 0
+    (moe.py:164-192).  Returns the accumulator dtype; round with bf16_round."""
+    rows = np.asarray(route_rows, dtype=np.int64).reshape(num_tokens, top_k)
+    padded = np.concatenate([np.asarray(y, dtype=accum), np.zeros((1, y.shape[1]), dtype=accum)])
+    safe = np.where((rows >= 0) & (rows < y.shape[0]), rows, y.shape[0])
+    out = np.zeros((num_tokens, y.shape[1]), dtype=accum)
+    for s in range(top_k):
+        out = (out + padded[safe[:, s]]).astype(accum)
+    return out
+
+
+def moe_forward(x: np.ndarray, logits: np.ndarray, w13: np.ndarray, w2: np.ndarray,
+                top_k: int, renormalize: bool, *, capacity: int | None = None,
+                num_local: int | None = None, expert_start: int = 0,
+                local_index: np.ndarray | None = None) -> dict:
+    """Full layer on one rank: route, capacity, local experts, combine."""
+    num_tokens, num_experts = logits.shape
+    num_local = w13.shape[0] if num_local is None else num_local
+    weights, ids = route_topk(logits, top_k, renormalize)
+    weights, ids, keep = apply_capacity(weights, ids, num_experts, capacity)
+    flat = ids.reshape(-1)
+    tokens = np.arange(flat.size) // top_k
+    y, computed = expert_rows(x, w13, w2, flat, weights.reshape(-1), tokens, num_experts,
+                              num_local, expert_start, local_index)
+    rows = np.where(computed, np.arange(flat.size), flat.size)
+    out = bf16_round(combine(y, rows, num_tokens, top_k))
+    return dict(weights=weights, ids=ids, keep=keep, y=y, output=out)
+
+
+# ---------------------------------------------------------------------------
+# The reference's own CPU path, restated for the CPU baseline timing:
+# _route + _forward_reference (moe.py:870-920, :546-580), bf16 torch ops.
+# ---------------------------------------------------------------------------
+def forward_reference_torch(x: torch.Tensor, gate_w: torch.Tensor, w13: torch.Tensor,
+                            w2: torch.Tensor, top_k: int, renormalize: bool,
+                            logits: torch.Tensor | None = None) -> torch.Tensor:
+    """Per-expert torch loop on CPU tensors (bf16), as the reference computes on CPU."""
+    if logits is None:
+        logits = torch.nn.functional.linear(x, gate_w)
+    probs = torch.softmax(logits, dim=-1, dtype=torch.float32)
+    w, ids = torch.topk(probs, top_k, dim=-1)
+    if renormalize:
+        w = w / w.sum(dim=-1, keepdim=True)
+    w = w.to(x.dtype)
+    out = torch.zeros_like(x)
+    inter = w13.shape[1] // 2
+    for e in ids.unique().tolist():
+        tok, slot = torch.where(ids == e)
+        gu = torch.nn.functional.linear(x[tok], w13[e])
+        h = torch.nn.functional.silu(gu[:, :inter]) * gu[:, inter:]
+        o = torch.nn.functional.linear(h, w2[e]) * w[tok, slot, None]
+        out.index_add_(0, tok, o)
+    return out

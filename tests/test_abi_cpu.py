@@ -1,0 +1,58 @@
+"""The C-ABI library loads without a GPU, exports every declared symbol, and
+rejects bad arguments before touching the device."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from extend_nano_vllm_b200 import _lib
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                      "include", "b200moe.h")
+
+
+def declared_symbols() -> list[str]:
+    text = open(HEADER).read()
+    return re.findall(r"B200MOE_API\s+[\w\s\*]+?\b(b200moe_\w+)\s*\(", text)
+
+
+def test_every_declared_symbol_is_exported_and_bound():
+    names = declared_symbols()
+    assert len(names) >= 15
+    lib = ctypes.CDLL(_lib.LIB_PATH)
+    for name in names:
+        assert hasattr(lib, name), name
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+    assert set(_lib.SIGNATURES) == set(names)
+
+
+def test_abi_version():
+    assert _lib.LIB.b200moe_abi_version() == 1
+
+
+def test_layout_sizes_match_reference_formulas():
+    # tests/test_moe_compact_layout.py:38: T=512, k=8, E=128 -> 6016 index rows.
+    assert _lib.LIB.b200moe_pack_row_capacity(4096, 128) == 6016
+    assert _lib.LIB.b200moe_pack_row_capacity(8, 128) == 128
+    assert _lib.LIB.b200moe_pack_max_mtiles(4096, 128) == 32 + 128
+    assert _lib.LIB.b200moe_pack_max_mtiles(8, 128) == 1 + 8
+    assert _lib.LIB.b200moe_pack_scratch_bytes(1024, 128) == 129 * 4
+    assert _lib.LIB.b200moe_pack_scratch_bytes(65536, 128) == 64 * 129 * 4
+
+
+def test_argument_errors_without_device():
+    null = ctypes.c_void_p(0)
+    with pytest.raises(ValueError, match="top_k"):
+        _lib.call("b200moe_route_topk", null, _lib.F32, 4, 8, 9, 1, null, null, null)
+    with pytest.raises(NotImplementedError, match="top_k"):
+        _lib.call("b200moe_route_topk", null, _lib.F32, 4, 64, 33, 1, null, null, null)
+    with pytest.raises(ValueError, match="num_local_experts"):
+        _lib.call("b200moe_pack_routes", null, null, 16, 8, null, 0, 9, null, -1, 32, null,
+                  null, null, null, null, null, null, 10, null, null, null, 0, null)
+    with pytest.raises(NotImplementedError, match="multiples of 16"):
+        _lib.call("b200moe_expert_gate_up", 0, null, 1, null, 24, 64, null, 1, null, null, 1, 1,
+                  16, null, 1, null, null, null)
+    with pytest.raises(ValueError, match="ep_size"):
+        _lib.call("b200moe_ep_plan", null, 1, 1, 8, null, 17, null, null, null, null)
