@@ -1,0 +1,497 @@
+#!/usr/bin/env python
+"""MoE-layer throughput of the B200 expert path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
+
+Headline workload (all N): the Qwen3-235B-A22B-shaped MoE layer (hidden 4096,
+128 experts, top-8, moe_intermediate 1536, bf16, weights N(0, 0.02)) with
+T = 4096 tokens per GPU; experts sharded over the N GPUs (128/N each) with
+the NCCL all-to-all backend for N > 1.  A step is one layer forward (router
+projection, softmax top-k, packing, grouped gate/up + SwiGLU, grouped down,
+exchange, combine) over that GPU's 4096 tokens.  ``value`` = tokens of all
+ranks per second with inputs resident in HBM; ``e2e`` adds, every step, the
+pinned host->device copy of the hidden states and the device->host copy of
+the output.  Timing: CUDA events on the launching stream, barrier +
+synchronize around the timed region, max over ranks.  Expert weights
+(4.83 GB / N per GPU) are larger than L2, so no extra L2 flush is needed.
+
+At N = 1, rank 0 also reports (``sweep``) the decode buckets T in
+{1, 8, 32, 64, 128, 256, 512} of the 30B-A3B layer (uniform fp32 logits, one
+CUDA graph per bucket, L2 flushed before every replay) and the T=8192
+chunked-prefill batch with Zipf(1.2) expert popularity and capacity factor
+1.25, each against its roofline; and a CPU baseline: the reference's own
+CPU algorithm (softmax/top-k and the per-expert torch loop of
+nanovllm/layers/moe.py:546-580, restated in oracle/) on a bounded sample.
+
+``--impl reference`` times that CPU implementation alone on the host cores
+(rank 0 only) on the same workload and prints the same line with
+"impl": "reference".
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+import torch.distributed as dist
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "MoE-layer tokens/s (Qwen3-235B-A22B-shaped layer, T=4096 tokens per GPU)"
+UNIT = "tokens/s"
+TOKENS_PER_GPU = 4096
+DECODE_BUCKETS = (1, 8, 32, 64, 128, 256, 512)
+PREFILL_TOKENS = 8192
+CPU_SAMPLE_TOKENS = 32
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--impl", choices=("native", "reference"), default="native")
+    p.add_argument("--no-sweep", action="store_true", help="skip the N=1 decode/prefill sweep")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def peaks() -> dict:
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            data = json.load(f)
+        return dict(hbm_gbs=float(data["hbm_gbs"]), bf16_tflops=float(data["bf16_tflops"]),
+                    bf16_tflops_sustained=float(data.get("bf16_tflops_sustained",
+                                                         data["bf16_tflops"])),
+                    source="measured")
+    return dict(hbm_gbs=6650.0, bf16_tflops=1590.0, bf16_tflops_sustained=1400.0,
+                source="fallback")
+
+
+# ---------------------------------------------------------------------------
+# Clocks sampled with nvidia-smi during a timed region.
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int) -> None:
+        self.gpu_index = gpu_index
+        self.proc = None
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-i", str(self.gpu_index), "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [r.split(",") for r in out.strip().splitlines() if r.strip()]
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            r = [c.strip() for c in r]
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, r[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+class KernelTimer:
+    """CUDA events around named launches on the current stream."""
+
+    def __init__(self) -> None:
+        self.events: dict[str, list] = {}
+        self.open: dict[str, torch.cuda.Event] = {}
+
+    def begin(self, name: str) -> None:
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        self.open[name] = ev
+
+    def end(self, name: str) -> None:
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        self.events.setdefault(name, []).append((self.open.pop(name), ev))
+
+    def mean_ms(self, name: str) -> float:
+        pairs = self.events.get(name, [])
+        return sum(a.elapsed_time(b) for a, b in pairs) / max(1, len(pairs))
+
+    def count(self, name: str) -> int:
+        return len(self.events.get(name, []))
+
+
+# ---------------------------------------------------------------------------
+# Distributed setup.
+# ---------------------------------------------------------------------------
+def init_dist(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        if world > 1 or args.gpus > 1:
+            raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch with torchrun")
+    if world > 1:
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                timeout=datetime.timedelta(seconds=300))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    t = torch.tensor([value], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int) -> None:
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+# ---------------------------------------------------------------------------
+# Native arm.
+# ---------------------------------------------------------------------------
+def build_layer(shape, world, rank, device, **kw):
+    import extend_nano_vllm_b200.workloads as wl
+    from extend_nano_vllm_b200 import ExpertParallelMoE
+
+    backend = "all_to_all_nvlink" if world > 1 else "replicated"
+    layer = ExpertParallelMoE(shape.hidden, shape.intermediate, shape.num_experts, shape.top_k,
+                              shape.norm_topk_prob, ep_rank=rank, ep_size=world,
+                              dispatch_backend=backend, **kw)
+    layer = layer.to(device=device, dtype=torch.bfloat16)
+    num_local = shape.num_experts // world
+    w13, w2 = wl.expert_weights(shape, seed=2024, num_local=num_local,
+                                first_expert=rank * num_local, device=device, on_device=True)
+    with torch.no_grad():
+        layer.gate.weight.copy_(wl.gate_weight(shape, seed=2025).to(device))
+        layer.gate_up_proj.copy_(w13)
+        layer.down_proj.copy_(w2)
+    del w13, w2
+    return layer
+
+
+def time_steps(fn, steps: int, warmup: int, world: int) -> float:
+    """Seconds for `steps` calls, max over ranks (events on the current stream)."""
+    for _ in range(warmup):
+        fn()
+    barrier(world)
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        fn()
+    stop.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    return max_over_ranks(start.elapsed_time(stop) / 1e3, world)
+
+
+def decode_sweep(steps: int, warmup: int, pk: dict) -> list[dict]:
+    import extend_nano_vllm_b200.workloads as wl
+    from extend_nano_vllm_b200 import STREAM_ENGINE_MAX_ROUTES
+
+    shape = wl.QWEN3_30B_A3B
+    device = torch.device("cuda")
+    layer = build_layer(shape, 1, 0, device, graph_safe_decode=True)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    results = []
+    for tokens in DECODE_BUCKETS:
+        x = wl.hidden_states(tokens, shape.hidden, seed=300 + tokens, device=device)
+        logits = wl.uniform_logits(tokens, shape.num_experts, seed=400 + tokens, device=device)
+        stream = torch.cuda.Stream()
+        stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                layer._forward_from_logits(x, logits)
+        torch.cuda.current_stream().wait_stream(stream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            layer._forward_from_logits(x, logits)
+        for _ in range(warmup):
+            graph.replay()
+        times = []
+        for _ in range(steps):
+            flush.fill_(1)  # evict the previous replay's weights from L2
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            graph.replay()
+            b.record()
+            times.append((a, b))
+        torch.cuda.synchronize()
+        ms = statistics.median(a.elapsed_time(b) for a, b in times)
+        ids = torch.topk(logits, shape.top_k, dim=-1).indices
+        active = int(torch.unique(ids).numel())
+        bytes_ = (active * shape.expert_bytes + tokens * shape.hidden * 2 * 2
+                  + tokens * shape.num_experts * 4)
+        achieved = bytes_ / (ms / 1e3) / 1e9
+        results.append({"tokens": tokens, "ms": round(ms, 5),
+                        "tokens_per_s": round(tokens / (ms / 1e3), 1),
+                        "active_experts": active, "algorithmic_bytes": bytes_,
+                        "achieved_gbs": round(achieved, 1),
+                        "hbm_roofline_frac": round(achieved / pk["hbm_gbs"], 4),
+                        "engine": ("stream" if tokens * shape.top_k <= STREAM_ENGINE_MAX_ROUTES
+                                   else "tcgen05")})
+        del graph
+    del layer, flush
+    torch.cuda.empty_cache()
+    return results
+
+
+def prefill_case(steps: int, warmup: int, pk: dict) -> dict:
+    import extend_nano_vllm_b200.workloads as wl
+
+    shape = wl.QWEN3_30B_A3B
+    device = torch.device("cuda")
+    layer = build_layer(shape, 1, 0, device, expert_capacity_factor=1.25)
+    x = wl.hidden_states(PREFILL_TOKENS, shape.hidden, seed=500, device=device)
+    logits = wl.zipf_logits(PREFILL_TOKENS, shape.num_experts, seed=501, device=device)
+    timer = KernelTimer()
+    fn = lambda: layer._forward_from_logits(x, logits)  # noqa: E731
+    for _ in range(warmup):
+        fn()
+    kept0 = layer.dispatch_assignment_count
+    layer.kernel_timer = timer
+    seconds = time_steps(fn, steps, 0, 1)
+    layer.kernel_timer = None
+    kept = (layer.dispatch_assignment_count - kept0) / steps
+    flops = kept * shape.flops_per_route
+    ms = seconds / steps * 1e3
+    gu_ms, dn_ms = timer.mean_ms("gate_up"), timer.mean_ms("down")
+    gu_flops = kept * 2 * 2 * shape.intermediate * shape.hidden
+    out = {"tokens": PREFILL_TOKENS, "capacity": wl.capacity_for(PREFILL_TOKENS, shape, 1.25),
+           "kept_routes": int(kept), "ms": round(ms, 4),
+           "tokens_per_s": round(PREFILL_TOKENS / (ms / 1e3), 1),
+           "layer_tflops": round(flops / (ms / 1e3) / 1e12, 1),
+           "layer_tensor_frac": round(flops / (ms / 1e3) / 1e12 / pk["bf16_tflops"], 4),
+           "gate_up_ms": round(gu_ms, 4), "down_ms": round(dn_ms, 4),
+           "gate_up_tflops": round(gu_flops / (gu_ms / 1e3) / 1e12, 1)}
+    del layer
+    torch.cuda.empty_cache()
+    return out
+
+
+def cpu_sample_rate(x_cpu, gate_cpu, w13_cpu, w2_cpu, shape, reps: int) -> tuple[float, int]:
+    """Tokens/s of the reference CPU algorithm over a bounded sample."""
+    from oracle import moe_oracle as mo
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    mo.forward_reference_torch(x_cpu[:4], gate_cpu, w13_cpu, w2_cpu, shape.top_k, True)
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        mo.forward_reference_torch(x_cpu, gate_cpu, w13_cpu, w2_cpu, shape.top_k, True)
+        times.append(time.perf_counter() - t0)
+    return x_cpu.size(0) / statistics.median(times), cores
+
+
+def native(args, world, rank, local) -> None:
+    import extend_nano_vllm_b200 as pkg
+    import extend_nano_vllm_b200.workloads as wl
+    from extend_nano_vllm_b200 import _lib
+
+    pk = peaks()
+    shape = wl.QWEN3_235B_A22B
+    device = torch.device("cuda", local)
+    layer = build_layer(shape, world, rank, device)
+    x = wl.hidden_states(TOKENS_PER_GPU, shape.hidden, seed=1000 + rank, device=device)
+    step = lambda: layer(x)  # noqa: E731
+
+    for _ in range(args.warmup):
+        step()
+    barrier(world)
+    kept0 = layer.dispatch_assignment_count
+    snapshot = dict(_lib.CALL_COUNTS)
+    timer = KernelTimer()
+    layer.kernel_timer = timer
+    clocks = ClockSampler(local)
+    clocks.start()
+    seconds = time_steps(step, args.steps, 0, world)
+    clock_info = clocks.stop()
+    layer.kernel_timer = None
+    launches = _lib.launches_since(snapshot)
+    kept_per_step = (layer.dispatch_assignment_count - kept0) / args.steps
+    ms_per_step = seconds / args.steps * 1e3
+    value = world * TOKENS_PER_GPU * args.steps / seconds
+
+    # Dominant kernel: the tcgen05 gate/up GEMM (2/3 of the FLOPs).
+    gu_ms = timer.mean_ms("gate_up")
+    gu_flops = kept_per_step * 2 * 2 * shape.intermediate * shape.hidden
+    gu_tflops = gu_flops / (gu_ms / 1e3) / 1e12 if gu_ms > 0 else 0.0
+    gu_tflops = max_over_ranks(gu_tflops, world) if world > 1 else gu_tflops
+    roofline = {"kernel": "grouped_gemm_kernel<gate_up> (tcgen05)", "bound": "tensor",
+                "achieved": round(gu_tflops, 1), "peak": pk["bf16_tflops_sustained"],
+                "peak_kind": f"bf16_tflops_sustained ({pk['source']})", "unit": "TFLOP/s",
+                "frac": round(gu_tflops / pk["bf16_tflops_sustained"], 4),
+                "traffic": None, "flops_per_launch": int(gu_flops),
+                "launch_ms": round(gu_ms, 4)}
+
+    # End to end through the public layer API with pinned host buffers.
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty((TOKENS_PER_GPU, shape.hidden), dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty_like(x)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        out = layer(x_dev)
+        out_host.copy_(out, non_blocking=True)
+
+    e2e_seconds = time_steps(e2e_step, args.steps, args.warmup, world)
+    e2e_value = world * TOKENS_PER_GPU * args.steps / e2e_seconds
+    h2d = x.numel() * x.element_size()
+
+    record = {
+        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) hidden, N(0,0.02) weights; no checkpoint)",
+        "config": {"workload": "configs[3]: Qwen3-235B-A22B-shaped MoE layer, EP over N GPUs",
+                   "hidden": shape.hidden, "num_experts": shape.num_experts,
+                   "top_k": shape.top_k, "moe_intermediate": shape.intermediate,
+                   "tokens_per_gpu": TOKENS_PER_GPU, "global_batch": world * TOKENS_PER_GPU,
+                   "parallelism": f"ep{world}",
+                   "exchange": "nccl all_to_all_single" if world > 1 else "none",
+                   "kept_routes_per_gpu_step": round(kept_per_step, 1),
+                   "l2": "inputs larger than L2 (expert weights %.2f GB per GPU)"
+                         % (shape.num_experts // world * shape.expert_bytes / 1e9)},
+        "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": h2d},
+        "gpu_launches": launches,
+        "roofline": roofline,
+        "clocks": clock_info,
+        "device_status": pkg.device_status(),
+    }
+    del layer, x, x_dev
+    torch.cuda.empty_cache()
+
+    if world == 1 and not args.no_sweep:
+        record["sweep"] = {"decode_30b_a3b": decode_sweep(max(20, args.steps // 4),
+                                                          args.warmup, pk),
+                           "prefill_30b_a3b_zipf": prefill_case(max(10, args.steps // 10),
+                                                                args.warmup, pk)}
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        layer_cpu = None
+        xs = wl.hidden_states(TOKENS_PER_GPU, shape.hidden, seed=1000)[:CPU_SAMPLE_TOKENS]
+        w13 = torch.empty((shape.num_experts, 2 * shape.intermediate, shape.hidden),
+                          dtype=torch.bfloat16)
+        w2 = torch.empty((shape.num_experts, shape.hidden, shape.intermediate),
+                         dtype=torch.bfloat16)
+        dev_w13, dev_w2 = wl.expert_weights(shape, seed=2024, device=device, on_device=True)
+        w13.copy_(dev_w13)
+        w2.copy_(dev_w2)
+        del dev_w13, dev_w2, layer_cpu
+        gate = wl.gate_weight(shape, seed=2025).to(torch.bfloat16)
+        rate, cores = cpu_sample_rate(xs, gate, w13, w2, shape, reps=3)
+        record["cpu_baseline"] = {
+            "value": round(rate, 2), "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{CPU_SAMPLE_TOKENS} tokens of the headline workload through the "
+                      "reference CPU algorithm (router + per-expert torch loop, bf16), "
+                      "median of 3"}
+    if rank == 0:
+        print(json.dumps(record), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# Reference arm: the reference's CPU implementation on the host cores.
+# ---------------------------------------------------------------------------
+def reference(args, world, rank) -> None:
+    if rank != 0:
+        return
+    import extend_nano_vllm_b200.workloads as wl
+
+    shape = wl.QWEN3_235B_A22B
+    x_all = wl.hidden_states(TOKENS_PER_GPU, shape.hidden, seed=1000)
+    w13, w2 = wl.expert_weights(shape, seed=2024)
+    gate = wl.gate_weight(shape, seed=2025).to(torch.bfloat16)
+    from oracle import moe_oracle as mo
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    # Size the per-step sample so warmup + steps take about 90 s in total.
+    t0 = time.perf_counter()
+    mo.forward_reference_torch(x_all[:8], gate, w13, w2, shape.top_k, True)
+    per_token = (time.perf_counter() - t0) / 8
+    budget = 90.0 / max(1, args.steps + args.warmup)
+    tokens = int(max(1, min(CPU_SAMPLE_TOKENS, budget // max(per_token, 1e-6))))
+    x = x_all[:tokens]
+    for _ in range(args.warmup):
+        mo.forward_reference_torch(x, gate, w13, w2, shape.top_k, True)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        mo.forward_reference_torch(x, gate, w13, w2, shape.top_k, True)
+    seconds = time.perf_counter() - t0
+    value = tokens * args.steps / seconds
+    sample = (f"{tokens} tokens of the headline workload per step through the reference "
+              "CPU algorithm (router + per-expert torch loop, bf16)")
+    record = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(seconds / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "configs[3]: Qwen3-235B-A22B-shaped MoE layer (CPU sample)",
+                   "tokens_per_step": tokens},
+        "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(record), flush=True)
+
+
+def main() -> None:
+    args = parse_args()
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        reference(args, int(os.environ.get("WORLD_SIZE", "1")), rank)
+        return
+    world, rank, local = init_dist(args)
+    try:
+        native(args, world, rank, local)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

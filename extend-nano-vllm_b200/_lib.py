@@ -47,7 +47,8 @@ SIGNATURES: dict[str, tuple] = {
     "b200moe_gather_rows": (_I, [_P, _L, _I, _P, _P, _I, _L, _L, _P, _P, _P]),
     "b200moe_expert_gate_up": (_I, [_I, _P, _L, _P, _I, _I, _P, _I, _P, _P, _I, _L, _L, _P,
                                     _L, _P, _P, _P]),
-    "b200moe_expert_down": (_I, [_I, _P, _I, _I, _P, _I, _P, _P, _L, _L, _P, _L, _P, _P, _P]),
+    "b200moe_expert_down": (_I, [_I, _P, _I, _I, _P, _I, _P, _P, _L, _L, _L, _P, _L, _P, _P,
+                                 _P]),
     "b200moe_combine": (_I, [_P, _L, _P, _L, _I, _I, _I, _P, _I, _P]),
     "b200moe_ep_plan": (_I, [_P, _L, _I, _I, _P, _I, _P, _P, _P, _P]),
     "b200moe_ep_pack": (_I, [_P, _I, _P, _P, _L, _I, _I, _P, _I, _P, _P, _P, _P, _P, _P, _P]),
@@ -82,8 +83,26 @@ def _load() -> ctypes.CDLL:
 LIB = _load()
 
 
+# Kernels each entry point launches (for launch accounting; the streaming
+# and tcgen05 engines both launch one kernel per projection).
+KERNELS_PER_CALL = {"b200moe_pack_routes": 2}
+# Calls made through call(), by entry-point name (launch accounting).
+CALL_COUNTS: dict[str, int] = {}
+
+
+def launches_since(snapshot: dict[str, int]) -> int:
+    """Kernels launched by library calls made after ``snapshot`` was taken."""
+    total = 0
+    for name, count in CALL_COUNTS.items():
+        if name.startswith("b200moe_device_status"):
+            continue
+        total += (count - snapshot.get(name, 0)) * KERNELS_PER_CALL.get(name, 1)
+    return total
+
+
 def call(name: str, *args) -> None:
     """Call an int-returning entry point and raise on a non-zero status."""
+    CALL_COUNTS[name] = CALL_COUNTS.get(name, 0) + 1
     rc = getattr(LIB, name)(*args)
     if rc != OK:
         message = LIB.b200moe_last_error().decode(errors="replace")

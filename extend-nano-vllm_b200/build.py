@@ -68,9 +68,20 @@ def _compile(src: str, extra: list[str]) -> str:
     return obj
 
 
+def _object_is_fresh(src: str) -> bool:
+    """An object is reused when newer than its source, the shared headers and this script."""
+    obj = os.path.join(BUILD_DIR, os.path.basename(src)[:-3] + ".o")
+    if not os.path.exists(obj):
+        return False
+    deps = [src, os.path.abspath(__file__)]
+    deps += [os.path.join(CSRC, n) for n in os.listdir(CSRC) if n.endswith(".cuh")]
+    deps += [os.path.join(INCLUDE, n) for n in os.listdir(INCLUDE)]
+    return os.path.getmtime(obj) >= max(os.path.getmtime(d) for d in deps)
+
+
 def build(force: bool = False, jobs: int | None = None, extra: list[str] | None = None,
           verbose: bool = False) -> str:
-    """Compile every kernel source and link LIB_PATH; returns the library path."""
+    """Compile the kernel sources that changed and link LIB_PATH; returns its path."""
     if not force and up_to_date():
         return LIB_PATH
     os.makedirs(BUILD_DIR, exist_ok=True)
@@ -79,8 +90,14 @@ def build(force: bool = False, jobs: int | None = None, extra: list[str] | None 
         extra += ["-Xptxas", "-v"]
     srcs = sources()
     jobs = jobs or min(len(srcs), os.cpu_count() or 4)
+
+    def obj_for(src: str) -> str:
+        if not force and not verbose and not extra and _object_is_fresh(src):
+            return os.path.join(BUILD_DIR, os.path.basename(src)[:-3] + ".o")
+        return _compile(src, extra)
+
     with concurrent.futures.ThreadPoolExecutor(max_workers=jobs) as pool:
-        objs = list(pool.map(lambda s: _compile(s, extra), srcs))
+        objs = list(pool.map(obj_for, srcs))
     tmp = LIB_PATH + ".tmp"
     cmd = [nvcc(), *ARCH_FLAGS, "-shared", "-rdc=true", "-cudart", "static", "-o", tmp, *objs]
     result = subprocess.run(cmd, capture_output=True, text=True)

@@ -9,11 +9,12 @@ int stream_gate_up(const void *x, int64_t x_rows, int hidden, int inter, const v
                    int64_t num_routes, const int32_t *mtiles, int64_t max_mtiles,
                    const int32_t *counters, void *act, cudaStream_t s);
 int stream_down(const void *act, int hidden, int inter, const void *w2, const int32_t *row_route,
-                const void *route_weights, int64_t num_routes, const int32_t *mtiles,
-                int64_t max_mtiles, const int32_t *counters, void *y, cudaStream_t s);
+                const void *route_weights, int64_t num_routes, int64_t max_expert_rows,
+                const int32_t *mtiles, int64_t max_mtiles, const int32_t *counters, void *y,
+                cudaStream_t s);
 int tc_gate_up(const void *x_packed, int hidden, int inter, const void *w13, int num_local,
-               int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
-               const int32_t *counters, void *act, cudaStream_t s);
+               int64_t num_routes, int64_t row_capacity, const int32_t *mtiles,
+               int64_t max_mtiles, const int32_t *counters, void *act, cudaStream_t s);
 int tc_down(const void *act, int hidden, int inter, const void *w2, int num_local,
             const int32_t *row_route, const void *route_weights, int64_t num_routes,
             int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
@@ -47,8 +48,8 @@ int b200moe_expert_gate_up(int engine, const void *x, int64_t x_rows, const void
   }
   if (engine == B200MOE_ENGINE_TCGEN05) {
     B200_ARG(x_packed != nullptr && aligned16(x_packed), "x_packed must be 16-byte aligned");
-    return tc_gate_up(x_packed, hidden, inter, w13, num_local_experts, row_capacity, mtiles,
-                      max_mtiles, counters, act, s);
+    return tc_gate_up(x_packed, hidden, inter, w13, num_local_experts, num_routes, row_capacity,
+                      mtiles, max_mtiles, counters, act, s);
   }
   set_error("unknown engine %d", engine);
   return B200MOE_EINVAL;
@@ -56,7 +57,8 @@ int b200moe_expert_gate_up(int engine, const void *x, int64_t x_rows, const void
 
 int b200moe_expert_down(int engine, const void *act, int hidden, int inter, const void *w2,
                         int num_local_experts, const int32_t *row_route,
-                        const void *route_weights, int64_t num_routes, int64_t row_capacity,
+                        const void *route_weights, int64_t num_routes, int64_t max_expert_rows,
+                        int64_t row_capacity,
                         const int32_t *mtiles, int64_t max_mtiles, const int32_t *counters,
                         void *y, void *stream) {
   using namespace b200moe;
@@ -69,8 +71,8 @@ int b200moe_expert_down(int engine, const void *act, int hidden, int inter, cons
   B200_ARG(aligned16(act) && aligned16(w2) && aligned16(y), "act, w2, y must be 16-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (engine == B200MOE_ENGINE_STREAM)
-    return stream_down(act, hidden, inter, w2, row_route, route_weights, num_routes, mtiles,
-                       max_mtiles, counters, y, s);
+    return stream_down(act, hidden, inter, w2, row_route, route_weights, num_routes,
+                       max_expert_rows, mtiles, max_mtiles, counters, y, s);
   if (engine == B200MOE_ENGINE_TCGEN05)
     return tc_down(act, hidden, inter, w2, num_local_experts, row_route, route_weights,
                    num_routes, row_capacity, mtiles, max_mtiles, counters, y, s);

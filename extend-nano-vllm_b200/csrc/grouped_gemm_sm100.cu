@@ -31,15 +31,20 @@ namespace b200moe {
 namespace tcg {
 
 constexpr int BM = 128;
-constexpr int BN = 256;
 constexpr int BK = 64;
-constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BK * 2;
-constexpr int B_BYTES = BN * BK * 2;
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int TMEM_COLS = 2 * BN;
 constexpr int THREADS = 192;
-constexpr size_t SMEM_BYTES = 1024 + static_cast<size_t>(STAGES) * STAGE_BYTES + 256;
+
+// Tile configuration for an N tile of BN columns (BN in {64, 128, 256}).
+template <int BN>
+struct Cfg {
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  // As many pipeline stages as fit in ~200 KB of shared memory (at most 8).
+  static constexpr int STAGES = (200 * 1024 / STAGE_BYTES) < 8 ? (200 * 1024 / STAGE_BYTES) : 8;
+  static constexpr int TMEM_COLS = 2 * BN;  // two accumulators
+  static constexpr size_t SMEM_BYTES = 1024 + static_cast<size_t>(STAGES) * STAGE_BYTES + 256;
+};
 
 struct Args {
   const int32_t *mtiles;
@@ -67,10 +72,14 @@ __device__ __forceinline__ void store16_bf16(__nv_bfloat16 *dst, const float (&v
   }
 }
 
-template <bool kGateUp>
+template <bool kGateUp, int BN>
 __global__ void __launch_bounds__(THREADS, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB, const Args args) {
+  constexpr int STAGES = Cfg<BN>::STAGES;
+  constexpr int B_BYTES = Cfg<BN>::B_BYTES;
+  constexpr int STAGE_BYTES = Cfg<BN>::STAGE_BYTES;
+  constexpr int TMEM_COLS = Cfg<BN>::TMEM_COLS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~static_cast<uintptr_t>(1023));
@@ -309,36 +318,45 @@ int make_map(CUtensorMap *map, const void *base, int rank, const uint64_t *dims,
   return B200MOE_OK;
 }
 
-template <bool kGateUp>
+template <bool kGateUp, int BN>
 int prepare_kernel() {
   static bool done[64] = {false};
   const int dev = current_device();
   if (dev >= 0 && dev < 64 && done[dev]) return B200MOE_OK;
-  B200_CUDA(cudaFuncSetAttribute(grouped_gemm_kernel<kGateUp>,
+  B200_CUDA(cudaFuncSetAttribute(grouped_gemm_kernel<kGateUp, BN>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(SMEM_BYTES)));
+                                 static_cast<int>(Cfg<BN>::SMEM_BYTES)));
   if (dev >= 0 && dev < 64) done[dev] = true;
   return B200MOE_OK;
 }
 
-template <bool kGateUp>
+template <bool kGateUp, int BN>
 int launch(const CUtensorMap &ma, const CUtensorMap &mb, const Args &args, cudaStream_t s) {
-  int rc = prepare_kernel<kGateUp>();
+  int rc = prepare_kernel<kGateUp, BN>();
   if (rc != B200MOE_OK) return rc;
   int64_t work = args.max_mtiles * args.n_tiles;
   int grid = sm_count();
   if (work < grid) grid = static_cast<int>(work);
   if (grid < 1) grid = 1;
-  grouped_gemm_kernel<kGateUp><<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb, args);
+  grouped_gemm_kernel<kGateUp, BN><<<grid, THREADS, Cfg<BN>::SMEM_BYTES, s>>>(ma, mb, args);
   B200_LAUNCHED();
   return B200MOE_OK;
 }
 
 }  // namespace tcg
 
-int tc_gate_up(const void *x_packed, int hidden, int inter, const void *w13, int num_local,
-               int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
-               const int32_t *counters, void *act, cudaStream_t s) {
+// N tile for a call: wide tiles for prefill-sized route counts, 128 for
+// decode buckets so the few active experts still cover every SM.  (64-wide
+// tiles measured slower: the 128-row A tile then dominates each stage.)
+int pick_bn(int64_t num_routes) {
+  if (num_routes > 4096) return 256;
+  return 128;
+}
+
+template <int BN>
+int tc_gate_up_bn(const void *x_packed, int hidden, int inter, const void *w13, int num_local,
+                  int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
+                  const int32_t *counters, void *act, cudaStream_t s) {
   using namespace tcg;
   CUtensorMap ma, mb;
   const uint64_t da[2] = {static_cast<uint64_t>(hidden), static_cast<uint64_t>(row_capacity)};
@@ -346,6 +364,7 @@ int tc_gate_up(const void *x_packed, int hidden, int inter, const void *w13, int
   const uint32_t ba[2] = {BK, BM};
   int rc = make_map(&ma, x_packed, 2, da, sa, ba);
   if (rc) return rc;
+  // W13 [E, 2I, H] viewed as [2E][I][H]: gate rows of expert e are slab 2e, up rows 2e+1.
   const uint64_t db[3] = {static_cast<uint64_t>(hidden), static_cast<uint64_t>(inter),
                           static_cast<uint64_t>(2) * num_local};
   const uint64_t sb[2] = {static_cast<uint64_t>(hidden) * 2,
@@ -364,13 +383,14 @@ int tc_gate_up(const void *x_packed, int hidden, int inter, const void *w13, int
   a.row_route = nullptr;
   a.route_w = nullptr;
   a.num_routes = 0;
-  return launch<true>(ma, mb, a, s);
+  return launch<true, BN>(ma, mb, a, s);
 }
 
-int tc_down(const void *act, int hidden, int inter, const void *w2, int num_local,
-            const int32_t *row_route, const void *route_weights, int64_t num_routes,
-            int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
-            const int32_t *counters, void *y, cudaStream_t s) {
+template <int BN>
+int tc_down_bn(const void *act, int hidden, int inter, const void *w2, int num_local,
+               const int32_t *row_route, const void *route_weights, int64_t num_routes,
+               int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
+               const int32_t *counters, void *y, cudaStream_t s) {
   using namespace tcg;
   CUtensorMap ma, mb;
   const uint64_t da[2] = {static_cast<uint64_t>(inter), static_cast<uint64_t>(row_capacity)};
@@ -396,7 +416,40 @@ int tc_down(const void *act, int hidden, int inter, const void *w2, int num_loca
   a.row_route = row_route;
   a.route_w = static_cast<const __nv_bfloat16 *>(route_weights);
   a.num_routes = num_routes;
-  return launch<false>(ma, mb, a, s);
+  return launch<false, BN>(ma, mb, a, s);
+}
+
+int tc_gate_up(const void *x_packed, int hidden, int inter, const void *w13, int num_local,
+               int64_t num_routes, int64_t row_capacity, const int32_t *mtiles,
+               int64_t max_mtiles, const int32_t *counters, void *act, cudaStream_t s) {
+  switch (pick_bn(num_routes)) {
+    case 256:
+      return tc_gate_up_bn<256>(x_packed, hidden, inter, w13, num_local, row_capacity, mtiles,
+                                max_mtiles, counters, act, s);
+    case 128:
+      return tc_gate_up_bn<128>(x_packed, hidden, inter, w13, num_local, row_capacity, mtiles,
+                                max_mtiles, counters, act, s);
+    default:
+      return tc_gate_up_bn<64>(x_packed, hidden, inter, w13, num_local, row_capacity, mtiles,
+                               max_mtiles, counters, act, s);
+  }
+}
+
+int tc_down(const void *act, int hidden, int inter, const void *w2, int num_local,
+            const int32_t *row_route, const void *route_weights, int64_t num_routes,
+            int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
+            const int32_t *counters, void *y, cudaStream_t s) {
+  switch (pick_bn(num_routes)) {
+    case 256:
+      return tc_down_bn<256>(act, hidden, inter, w2, num_local, row_route, route_weights,
+                             num_routes, row_capacity, mtiles, max_mtiles, counters, y, s);
+    case 128:
+      return tc_down_bn<128>(act, hidden, inter, w2, num_local, row_route, route_weights,
+                             num_routes, row_capacity, mtiles, max_mtiles, counters, y, s);
+    default:
+      return tc_down_bn<64>(act, hidden, inter, w2, num_local, row_route, route_weights,
+                            num_routes, row_capacity, mtiles, max_mtiles, counters, y, s);
+  }
 }
 
 }  // namespace b200moe

@@ -37,8 +37,9 @@ from . import ops as _native_ops
 _MOE_BLOCK_M = _lib.BLOCK_ROWS
 MOE_MAX_GRAPH_TOKENS_PER_RANK = 512
 # Routes per call up to which the weight-streaming engine runs (decode
-# buckets of <= 16 tokens at top-8); above it the tcgen05 grouped GEMM runs.
-STREAM_ENGINE_MAX_ROUTES = 128
+# buckets of <= 2 tokens at top-8, measured crossover); above it the tcgen05
+# grouped GEMM runs.
+STREAM_ENGINE_MAX_ROUTES = 16
 
 DISPATCH_BACKENDS = (
     "replicated", "all_to_all", "all_to_all_reduce",
@@ -220,6 +221,9 @@ class ExpertParallelMoE(nn.Module):
         self._ops = _native_ops
         # "auto" | "stream" | "tcgen05": expert GEMM engine selection.
         self.expert_engine = "auto"
+        # Optional object with begin(name)/end(name) that records CUDA events
+        # around the grouped GEMM launches (used by the benchmark).
+        self.kernel_timer = None
         self.ep_all_reduce_count = 0
         self.ep_reduce_scatter_count = 0
         self.ep_all_gather_count = 0
@@ -437,14 +441,22 @@ class ExpertParallelMoE(nn.Module):
         """Grouped gate/up + SwiGLU and grouped down -> y [num_routes, H] (route order)."""
         engine = self._engine(packed.num_routes)
         ops = self._ops
+        timer = self.kernel_timer
         if engine == _lib.ENGINE_STREAM:
-            act = ops.expert_gate_up(engine, x, None, self.gate_up_proj, packed, top_k,
-                                     token_of_route)
+            x_packed = None
         else:
             x_packed = ops.gather_rows(x, packed, top_k, token_of_route)
-            act = ops.expert_gate_up(engine, x, x_packed, self.gate_up_proj, packed, top_k,
-                                     token_of_route)
-        return ops.expert_down(engine, act, self.down_proj, packed, flat_weights)
+        if timer is not None:
+            timer.begin("gate_up")
+        act = ops.expert_gate_up(engine, x, x_packed, self.gate_up_proj, packed, top_k,
+                                 token_of_route)
+        if timer is not None:
+            timer.end("gate_up")
+            timer.begin("down")
+        y = ops.expert_down(engine, act, self.down_proj, packed, flat_weights, x.size(0))
+        if timer is not None:
+            timer.end("down")
+        return y
 
     def _output_dtype(self, dtype: torch.dtype) -> torch.dtype:
         return torch.float64 if self.fp64_combine else torch.float32 if self.fp32_reduce else dtype
@@ -515,12 +527,18 @@ class ExpertParallelMoE(nn.Module):
     # ------------------------------------------------------------------
     def _forward_local(self, x: torch.Tensor) -> torch.Tensor:
         """Route + capacity + local experts + combine, no host synchronisation."""
+        if x.size(0) == 0:
+            return torch.zeros_like(x)
+        return self._forward_from_logits(x, self.gate(x))
+
+    def _forward_from_logits(self, x: torch.Tensor, logits: torch.Tensor) -> torch.Tensor:
+        """The expert path from given router logits [T, E] (fp32, bf16 or fp16):
+        softmax top-k, capacity, packing, grouped GEMMs and combine."""
         num_tokens = x.size(0)
         if num_tokens == 0:
             return torch.zeros_like(x)
         self._check_inputs(x)
         stats = self._device_stats(x.device)
-        logits = self.gate(x)
         weights, ids = self._ops.route_topk(logits, self.top_k, self.norm_topk_prob)
         flat_w = weights.view(-1)
         packed = self._pack(ids.view(-1), flat_w, capacity=self._capacity(num_tokens),

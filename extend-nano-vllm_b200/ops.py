@@ -154,7 +154,7 @@ def expert_gate_up(engine: int, x: torch.Tensor, x_packed: torch.Tensor | None,
 
 
 def expert_down(engine: int, act: torch.Tensor, w2: torch.Tensor, packed: PackedRoutes,
-                route_weights: torch.Tensor) -> torch.Tensor:
+                route_weights: torch.Tensor, max_expert_rows: int = 0) -> torch.Tensor:
     """Route-weighted down projection -> y [num_routes, H] in route order.
 
     Rows of routes that are not computed here are left unwritten; combine masks
@@ -163,8 +163,9 @@ def expert_down(engine: int, act: torch.Tensor, w2: torch.Tensor, packed: Packed
     num_local, hidden, inter = w2.shape
     y = torch.empty((packed.num_routes, hidden), device=act.device, dtype=torch.bfloat16)
     call("b200moe_expert_down", engine, _p(act), hidden, inter, _p(w2), num_local,
-         _p(packed.row_route), _p(route_weights), packed.num_routes, packed.row_capacity,
-         _p(packed.mtiles), packed.max_mtiles, _p(packed.counters), _p(y), _stream(act))
+         _p(packed.row_route), _p(route_weights), packed.num_routes, int(max_expert_rows),
+         packed.row_capacity, _p(packed.mtiles), packed.max_mtiles, _p(packed.counters), _p(y),
+         _stream(act))
     return y
 
 

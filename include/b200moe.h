@@ -186,10 +186,14 @@ B200MOE_API int b200moe_expert_gate_up(int engine, const void *x, int64_t x_rows
  *   w2  [E_loc, H, I] bf16;  route_weights [num_routes] bf16;
  *   y   [num_routes, H] bf16 out in route order (rows of routes not computed
  *       here are not written; combine masks them through combine_rows).
+ *   max_expert_rows: upper bound on the rows of one expert (the token rows of
+ *       the call: a token has at most one route per expert), or 0 if unknown;
+ *       lets the streaming engine pick a register-lean variant.
  */
 B200MOE_API int b200moe_expert_down(int engine, const void *act, int hidden, int inter, const void *w2,
                         int num_local_experts, const int32_t *row_route,
-                        const void *route_weights, int64_t num_routes, int64_t row_capacity,
+                        const void *route_weights, int64_t num_routes, int64_t max_expert_rows,
+                        int64_t row_capacity,
                         const int32_t *mtiles, int64_t max_mtiles, const int32_t *counters,
                         void *y, void *stream);
 

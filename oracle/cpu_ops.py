@@ -110,7 +110,7 @@ class CpuOps:
             act[torch.from_numpy(rows[sel])] = _bf16(s * u)
         return act
 
-    def expert_down(self, engine, act, w2, packed, route_weights):
+    def expert_down(self, engine, act, w2, packed, route_weights, max_expert_rows=0):
         H = w2.shape[1]
         y = torch.zeros((packed.num_routes, H), dtype=torch.bfloat16)
         rows = np.nonzero(packed.row_route.numpy() < packed.num_routes)[0]

@@ -198,7 +198,7 @@ def _expert_case(shape, tokens, engine, seed, logits_kind="uniform", capacity=No
     else:
         xp = ops.gather_rows(xd, p, shape.top_k)
         act = ops.expert_gate_up(engine, xd, xp, w13d, p, shape.top_k)
-    y = ops.expert_down(engine, act, w2d, p, w.view(-1))
+    y = ops.expert_down(engine, act, w2d, p, w.view(-1), tokens)
     out = ops.combine(y, p.combine_rows, tokens, shape.top_k)
     torch.cuda.synchronize()
     np.testing.assert_array_equal(ids.cpu().numpy(), res["ids"])
