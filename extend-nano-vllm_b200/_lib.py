@@ -43,6 +43,9 @@ SIGNATURES: dict[str, tuple] = {
     "b200moe_pack_max_mtiles": (_L, [_L, _I]),
     "b200moe_pack_routes": (_I, [_P, _P, _L, _I, _P, _I, _I, _P, _L, _L, _P, _P, _P, _P, _P,
                                  _P, _P, _L, _P, _P, _P, _S, _P]),
+    "b200moe_pack_static_scratch_capacity": (_S, []),
+    "b200moe_pack_routes_static_scratch": (_I, [_P, _P, _L, _I, _P, _I, _I, _P, _L, _L, _P, _P,
+                                                _P, _P, _P, _P, _P, _L, _P, _P, _P]),
     "b200moe_expert_histogram": (_I, [_P, _L, _I, _P, _P]),
     "b200moe_gather_rows": (_I, [_P, _L, _I, _P, _P, _I, _L, _L, _P, _P, _P]),
     "b200moe_expert_gate_up": (_I, [_I, _P, _L, _P, _I, _I, _P, _I, _P, _P, _I, _L, _L, _P,
@@ -85,7 +88,7 @@ LIB = _load()
 
 # Kernels each entry point launches (for launch accounting; the streaming
 # and tcgen05 engines both launch one kernel per projection).
-KERNELS_PER_CALL = {"b200moe_pack_routes": 2}
+KERNELS_PER_CALL = {"b200moe_pack_routes": 2, "b200moe_pack_routes_static_scratch": 2}
 # Calls made through call(), by entry-point name (launch accounting).
 CALL_COUNTS: dict[str, int] = {}
 

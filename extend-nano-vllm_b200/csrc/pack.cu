@@ -435,3 +435,78 @@ int b200moe_expert_histogram(const int64_t *expert_ids, int64_t num_routes, int 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Packing without caller-provided scratch.
+//
+// Some callers cannot hand this library a scratch buffer: embedders that have
+// already given almost all device memory to their own fixed-size pools (for
+// example a KV-cache arena that reserves the remaining HBM at start-up), and
+// plain C / FFI hosts with no device allocator of their own.  For them the
+// per-block histograms of b200moe_pack_routes live in one file-scope device
+// array instead.  That array is part of the library image: every GPU that
+// loads the library holds it (kPackStaticScratchBytes) until the process
+// exits, and nothing is allocated at call time.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace b200moe {
+namespace {
+
+constexpr size_t kPackStaticScratchBytes = 256 * 1024;
+static __device__ __align__(256) int32_t g_pack_static_scratch[kPackStaticScratchBytes / 4];
+
+std::mutex g_static_scratch_mutex;
+void *g_static_scratch_addr[64] = {nullptr};
+
+// Device address of the static array on the current device.  The first call
+// on a device looks it up with cudaGetSymbolAddress (that device current);
+// later calls reuse the cached address.
+int static_scratch_address(void **out) {
+  const int dev = current_device();
+  if (dev < 0 || dev >= 64) {
+    set_error("device ordinal %d out of range for the static scratch table", dev);
+    return B200MOE_EUNSUPPORTED;
+  }
+  std::lock_guard<std::mutex> lock(g_static_scratch_mutex);
+  if (g_static_scratch_addr[dev] == nullptr) {
+    void *p = nullptr;
+    B200_CUDA(cudaGetSymbolAddress(&p, g_pack_static_scratch));
+    g_static_scratch_addr[dev] = p;
+  }
+  *out = g_static_scratch_addr[dev];
+  return B200MOE_OK;
+}
+
+}  // namespace
+}  // namespace b200moe
+
+extern "C" {
+
+size_t b200moe_pack_static_scratch_capacity(void) { return b200moe::kPackStaticScratchBytes; }
+
+int b200moe_pack_routes_static_scratch(
+    int64_t *expert_ids, void *route_weights, int64_t num_routes, int num_experts,
+    const int64_t *local_index, int expert_start, int num_local_experts,
+    const int32_t *expert_base, int64_t capacity, int64_t row_capacity, int32_t *row_route,
+    int32_t *route_row, int32_t *combine_rows, int32_t *tile_expert, int32_t *expert_offsets,
+    int32_t *expert_counts, int32_t *mtiles, int64_t max_mtiles, int32_t *counters,
+    int64_t *stats, void *stream) {
+  const size_t need = b200moe_pack_scratch_bytes(num_routes, num_experts);
+  B200_ARG(need <= b200moe::kPackStaticScratchBytes,
+           "%lld routes over %d experts need %zu scratch bytes; the static scratch holds %zu "
+           "(use b200moe_pack_routes with a caller buffer)",
+           (long long)num_routes, num_experts, need, b200moe::kPackStaticScratchBytes);
+  void *scratch = nullptr;
+  const int rc = b200moe::static_scratch_address(&scratch);
+  if (rc != B200MOE_OK) return rc;
+  // The histogram kernel writes every word the scatter kernel reads, so the
+  // array needs no clearing between calls.
+  return b200moe_pack_routes(expert_ids, route_weights, num_routes, num_experts, local_index,
+                             expert_start, num_local_experts, expert_base, capacity,
+                             row_capacity, row_route, route_row, combine_rows, tile_expert,
+                             expert_offsets, expert_counts, mtiles, max_mtiles, counters, stats,
+                             scratch, b200moe::kPackStaticScratchBytes, stream);
+}
+
+}  // extern "C"

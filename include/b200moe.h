@@ -140,6 +140,37 @@ B200MOE_API int b200moe_pack_routes(int64_t *expert_ids, void *route_weights, in
                         void *scratch, size_t scratch_bytes, void *stream);
 
 /*
+ * b200moe_pack_routes for callers that cannot provide scratch memory.  No
+ * counterpart in the reference: it exists for hosts that have committed
+ * (nearly) all device memory to their own fixed pools, or that drive this
+ * library from plain C / FFI without a device allocator, so the histogram
+ * scratch of the packing kernels comes from a static device array inside the
+ * library instead of a caller buffer.
+ *  - Same arguments and results as b200moe_pack_routes, minus scratch.
+ *  - Limit: b200moe_pack_static_scratch_capacity() bytes (256 KiB), i.e.
+ *    b200moe_pack_scratch_bytes(num_routes, num_experts) must not exceed it;
+ *    every call with up to 65,536 routes and up to 1,023 experts fits, and
+ *    at 128 experts any route count up to 520,192 does.  Larger calls fail
+ *    with B200MOE_EINVAL and a message.  Each GPU that loads the library
+ *    holds the array until the process exits.
+ *  - Allocates nothing: no cudaMalloc/cudaFree.  The first call on each
+ *    device looks up the array's device address (cudaGetSymbolAddress) with
+ *    that device current; make that first call before any stream capture.
+ *  - All calls on a device share the one array and every call overwrites the
+ *    part it uses (nothing needs to start at zero); calls whose kernels
+ *    overlap on the GPU (different streams without ordering) race and must be
+ *    serialised by the caller.
+ */
+B200MOE_API size_t b200moe_pack_static_scratch_capacity(void);
+B200MOE_API int b200moe_pack_routes_static_scratch(
+    int64_t *expert_ids, void *route_weights, int64_t num_routes, int num_experts,
+    const int64_t *local_index, int expert_start, int num_local_experts,
+    const int32_t *expert_base, int64_t capacity, int64_t row_capacity, int32_t *row_route,
+    int32_t *route_row, int32_t *combine_rows, int32_t *tile_expert, int32_t *expert_offsets,
+    int32_t *expert_counts, int32_t *mtiles, int64_t max_mtiles, int32_t *counters,
+    int64_t *stats, void *stream);
+
+/*
  * Per-expert route counts of a flat route array: counts[e] for e < num_experts
  * (ids outside the range are ignored).  Used by the expert-parallel exchange to
  * agree on global capacity positions (the reference routes the gathered global
