@@ -62,7 +62,27 @@ def parse_args():
     p.add_argument("--impl", choices=("native", "reference"), default="native")
     p.add_argument("--no-sweep", action="store_true", help="skip the N=1 decode/prefill sweep")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--profile-case", choices=("gemm-small",), default=None,
+                   help="run a small case for ncu captures and exit (no JSON line): "
+                        "gemm-small = 235B-shaped experts, 16 experts x 320 routed rows, "
+                        "604 MB of weights (larger than L2), --steps forwards")
     return p.parse_args()
+
+
+def profile_case(args) -> None:
+    """Small workload with the headline's per-expert structure, for ncu."""
+    import extend_nano_vllm_b200.workloads as wl
+
+    torch.cuda.set_device(0)
+    device = torch.device("cuda", 0)
+    shape = wl.LayerShape("profile-small", 4096, 1536, 16, 8)
+    layer = build_layer(shape, 1, 0, device)
+    x = wl.hidden_states(640, shape.hidden, seed=3, device=device)
+    for _ in range(max(1, args.steps)):
+        layer(x)
+    torch.cuda.synchronize()
+    print(f"profile case {args.profile_case}: {args.steps} forwards, "
+          f"{layer.dispatch_assignment_count} routes", flush=True)
 
 
 def peaks() -> dict:
@@ -481,6 +501,9 @@ def reference(args, world, rank) -> None:
 
 def main() -> None:
     args = parse_args()
+    if args.profile_case:
+        profile_case(args)
+        return
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))
         reference(args, int(os.environ.get("WORLD_SIZE", "1")), rank)

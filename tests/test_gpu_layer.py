@@ -1,0 +1,238 @@
+"""Layer-level GPU tests of ExpertParallelMoE, modelled on the reference's
+layer tests (tests/test_moe_graph_capture.py, test_moe_compact_layout.py,
+test_moe_precision_mode.py, test_moe_capacity.py, test_moe_kernel.py).
+Tolerances as in test_gpu_kernels.py: layer outputs max|diff| <= 1e-2*max|ref|,
+mean <= 1e-3*max|ref|; integer results and combines bit-exact."""
+
+import numpy as np
+import pytest
+import torch
+
+import extend_nano_vllm_b200.workloads as wl
+from extend_nano_vllm_b200 import _lib
+from extend_nano_vllm_b200.moe import ExpertParallelMoE
+from oracle import moe_oracle as mo
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda")
+
+
+def close(got: torch.Tensor, ref, max_rel=1e-2, mean_rel=1e-3):
+    got = got.float().cpu().numpy()
+    ref = ref.float().cpu().numpy() if isinstance(ref, torch.Tensor) else ref
+    scale = float(np.abs(ref).max()) or 1.0
+    diff = np.abs(got.astype(np.float64) - ref)
+    assert diff.max() <= max_rel * scale, (diff.max(), scale)
+    assert diff.mean() <= mean_rel * scale, (diff.mean(), scale)
+
+
+def make_layer(shape, seed, **kw):
+    layer = ExpertParallelMoE(shape.hidden, shape.intermediate, shape.num_experts, shape.top_k,
+                              shape.norm_topk_prob, **kw).to(device=DEV, dtype=torch.bfloat16)
+    w13, w2 = wl.expert_weights(shape, seed=seed, num_local=layer.num_local_experts,
+                                first_expert=max(layer.expert_start, 0))
+    gate = wl.gate_weight(shape, seed=seed + 1).to(torch.bfloat16)
+    with torch.no_grad():
+        layer.gate.weight.copy_(gate)
+        layer.gate_up_proj.copy_(w13)
+        layer.down_proj.copy_(w2)
+    return layer, w13, w2, gate
+
+
+@pytest.fixture(autouse=True)
+def clean_status():
+    _lib.device_status(clear=True)
+    yield
+    assert _lib.device_status(clear=True) == 0
+
+
+SMALL = wl.LayerShape("small", 128, 256, 8, 2)
+A = wl.QWEN3_30B_A3B
+
+
+@pytest.mark.parametrize("tokens", [1, 4, 16, 17, 32])
+@torch.inference_mode()
+def test_decode_cuda_graph_replays_changed_inputs(tokens):
+    layer, *_ = make_layer(SMALL, 17, graph_safe_decode=True)
+    hidden = wl.hidden_states(tokens, 128, seed=1).to(DEV)
+    first, second = hidden.clone(), wl.hidden_states(tokens, 128, seed=2).to(DEV)
+    expected_first, expected_second = layer(first), layer(second)
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        layer(hidden)
+    torch.cuda.current_stream().wait_stream(stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        output = layer(hidden)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(output, expected_first)
+    hidden.copy_(second)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(output, expected_second)
+    assert not torch.equal(expected_first, expected_second)
+
+
+@torch.inference_mode()
+def test_layer_matches_oracle_config1_shape_and_counters():
+    layer, w13, w2, gate = make_layer(A, 31)
+    x = wl.hidden_states(64, A.hidden, seed=33)
+    out = layer(x.to(DEV))
+    logits = torch.nn.functional.linear(x, gate).float().numpy()
+    ref = mo.moe_forward(x.float().numpy(), logits, w13.float().numpy(), w2.float().numpy(), 8,
+                         True)
+    close(out, ref["output"])
+    assert layer.dispatch_assignment_count == 64 * 8
+    assert layer.total_assignment_count == 64 * 8
+
+
+@torch.inference_mode()
+def test_capacity_counters_match_oracle():
+    layer, w13, w2, gate = make_layer(A, 41, expert_capacity_factor=0.5)
+    x = wl.hidden_states(256, A.hidden, seed=43)
+    out = layer(x.to(DEV))
+    logits = torch.nn.functional.linear(x, gate).float().numpy()
+    cap = mo.capacity_of(256, 8, 128, None, 0.5)
+    ref = mo.moe_forward(x.float().numpy(), logits, w13.float().numpy(), w2.float().numpy(), 8,
+                         True, capacity=cap)
+    close(out, ref["output"])
+    kept = int(ref["keep"].sum())
+    assert layer.dispatch_assignment_count == kept
+    assert layer.dropped_assignment_count == 256 * 8 - kept > 0
+
+
+@pytest.mark.parametrize("tokens", [1, 4, 16, 17, 32])
+@torch.inference_mode()
+def test_static_decode_matches_dynamic_local_expert_shards(tokens):
+    hidden = wl.hidden_states(tokens, 128, seed=100 + tokens).to(DEV)
+    shape = wl.LayerShape("shard", 128, 256, 128, 8)
+    for ep_rank in range(4):
+        module, *_ = make_layer(shape, 5, ep_rank=ep_rank, ep_size=4)
+        weights, experts = module._route(hidden)
+        dynamic, dynamic_count = module._execute_local(hidden, weights, experts)
+        module.graph_safe_decode = True
+        static, static_count = module._execute_local(hidden, weights, experts)
+        assert static_count == dynamic_count
+        assert torch.equal(static, dynamic)
+
+
+@torch.inference_mode()
+def test_ep_shard_partials_sum_to_unsharded_layer():
+    # Simulated EP=2 on one GPU (reference tests/test_moe_kernel.py:64-86).
+    full, *_ = make_layer(SMALL, 21)
+    x = wl.hidden_states(22, 128, seed=23).to(DEV)
+    weights, experts = full._route(x)
+    reference, count = full._execute_local(x, weights, experts)
+    parts, total = [], 0
+    for rank in range(2):
+        shard = ExpertParallelMoE(128, 256, 8, 2, True, rank, 2).to(device=DEV,
+                                                                   dtype=torch.bfloat16)
+        with torch.no_grad():
+            shard.gate.weight.copy_(full.gate.weight)
+            shard.gate_up_proj.copy_(full.gate_up_proj[4 * rank:4 * rank + 4])
+            shard.down_proj.copy_(full.down_proj[4 * rank:4 * rank + 4])
+        out, n = shard._execute_local(x, weights, experts)
+        parts.append(out.float())
+        total += n
+    assert total == count == 22 * 2
+    close(parts[0] + parts[1], reference.float())
+
+
+@torch.inference_mode()
+def test_expert_with_more_than_one_tile_and_graph():
+    module, *_ = make_layer(SMALL, 132)
+    hidden = wl.hidden_states(300, 128, seed=3).to(DEV)
+    selected = torch.tensor([0, 1], device=DEV).expand(300, 2)
+    weights = torch.full((300, 2), 0.5, device=DEV, dtype=torch.bfloat16)
+    dynamic, _ = module._forward_triton(hidden, weights, selected)
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        module._forward_static_decode(hidden, weights, selected)
+    torch.cuda.current_stream().wait_stream(stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        replayed, _ = module._forward_static_decode(hidden, weights, selected)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(replayed, dynamic)
+    hidden.copy_(wl.hidden_states(300, 128, seed=4).to(DEV))
+    expected, _ = module._forward_triton(hidden, weights, selected)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(replayed, expected)
+
+
+@pytest.mark.parametrize("static_decode", [False, True])
+@torch.inference_mode()
+def test_moe_combine_is_exactly_repeatable(static_decode):
+    module, *_ = make_layer(wl.LayerShape("rep", 128, 256, 8, 8), 17)
+    hidden = wl.hidden_states(16, 128, seed=5).to(DEV)
+    selected = torch.arange(8, device=DEV).expand(16, 8)
+    weights = torch.full((16, 8), 0.125, device=DEV, dtype=torch.bfloat16)
+    forward = module._forward_static_decode if static_decode else module._forward_triton
+    outputs = [forward(hidden, weights, selected)[0] for _ in range(8)]
+    assert all(torch.equal(o, outputs[0]) for o in outputs[1:])
+
+
+def test_route_order_combine_handles_missing_and_permuted_routes():
+    torch.manual_seed(23)
+    module = ExpertParallelMoE(32, 64, 8, 4, True)
+    packed = torch.randn(9, 32, dtype=torch.bfloat16)
+    route_rows = torch.tensor([3, 0, 9, 7, 2, 9, 8, 1, 4, 9, 6, 5], dtype=torch.int32)
+    expected = torch.cat((packed, torch.zeros_like(packed[:1])))[route_rows.long()].reshape(
+        3, 4, 32).float().sum(dim=1).bfloat16()
+    actual = module._combine_expert_routes(packed.to(DEV), route_rows.to(DEV), 3, 4)
+    assert torch.equal(actual.cpu(), expected)
+
+
+def test_fp32_and_fp64_combine_precision_modes(monkeypatch):
+    monkeypatch.setenv("NANOVLLM_EXPERIMENTAL_FP32_EP_REDUCE", "1")
+    module = ExpertParallelMoE(16, 32, 8, 2, True, ep_rank=0, ep_size=4)
+    y = torch.tensor([[1.0] * 16, [0.00390625] * 16], dtype=torch.bfloat16, device=DEV)
+    out = module._combine_expert_routes(y, torch.tensor([0, 1], dtype=torch.int32, device=DEV),
+                                        1, 2)
+    assert out.dtype == torch.float32
+    assert torch.equal(out.cpu(), torch.full((1, 16), 1.00390625))
+    monkeypatch.delenv("NANOVLLM_EXPERIMENTAL_FP32_EP_REDUCE")
+    monkeypatch.setenv("NANOVLLM_EXPERIMENTAL_FP64_MOE_COMBINE", "1")
+    module = ExpertParallelMoE(16, 32, 8, 8, True, ep_rank=0, ep_size=4)
+    values = torch.tensor([0.043701171875, 0.037109375, -0.0047607421875, -0.00506591796875,
+                           -4.423782229423523e-09, -0.001953125, 0.005859375,
+                           -0.01068115234375], dtype=torch.bfloat16)
+    values = values.unsqueeze(1).expand(8, 16).contiguous()
+    out = module._combine_expert_routes(values.to(DEV), torch.arange(8, dtype=torch.int32,
+                                                                     device=DEV), 1, 8)
+    assert out.dtype == torch.float64
+    assert torch.equal(out.cpu(), values.double().sum(dim=0, keepdim=True))
+
+
+def test_cuda_route_mapping_replays_changed_input():
+    layer = ExpertParallelMoE(16, 32, 4, 2, True, ep_rank=0, ep_size=2,
+                              expert_owners=[0, 1, 1, 0]).to(DEV)
+    routes = torch.tensor([-1, 0, 1, 2, 3, 4], device=DEV)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        mask, local_ids = layer._local_routes(routes)
+    for values, expected_mask, expected_ids in (
+        ([-1, 0, 1, 2, 3, 4], [False, True, False, False, True, False], [0, 1]),
+        ([4, 1, 3, 0, 2, -1], [False, False, True, True, False, False], [1, 0]),
+    ):
+        routes.copy_(torch.tensor(values, device=DEV))
+        graph.replay()
+        torch.cuda.synchronize()
+        assert mask.tolist() == expected_mask
+        assert local_ids[mask].tolist() == expected_ids
+
+
+@torch.inference_mode()
+def test_relocate_experts_single_rank_keeps_storage():
+    layer, *_ = make_layer(SMALL, 9, dynamic_placement=True)
+    ptr = layer.gate_up_proj.data_ptr()
+    x = wl.hidden_states(12, 128, seed=1).to(DEV)
+    before = layer(x)
+    assert layer.relocate_experts(tuple(range(1)) * 8) == 0
+    assert layer.gate_up_proj.data_ptr() == ptr
+    assert torch.equal(layer(x), before)
