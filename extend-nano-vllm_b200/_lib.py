@@ -20,7 +20,7 @@ ECUDA = 2
 EUNSUPPORTED = 3
 
 BF16, F16, F32, F64 = 0, 1, 2, 3
-ENGINE_STREAM, ENGINE_TCGEN05 = 0, 1
+ENGINE_STREAM, ENGINE_TCGEN05, ENGINE_TCGEN05_WIDE, ENGINE_TCGEN05_SWAP = 0, 1, 2, 3
 MTILE_WORDS = 3
 MTILE_ROWS = 128
 BLOCK_ROWS = 16

@@ -19,9 +19,25 @@ int tc_down(const void *act, int hidden, int inter, const void *w2, int num_loca
             const int32_t *row_route, const void *route_weights, int64_t num_routes,
             int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
             const int32_t *counters, void *y, cudaStream_t s);
+int tcs_gate_up(const void *x_packed, int hidden, int inter, const void *w13, int num_local,
+                int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
+                const int32_t *counters, void *act, cudaStream_t s);
+int tcs_down(const void *act, int hidden, int inter, const void *w2, int num_local,
+             const int32_t *row_route, const void *route_weights, int64_t num_routes,
+             int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
+             const int32_t *counters, void *y, cudaStream_t s);
 
 namespace {
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ENGINE_TCGEN05 picks the tcgen05 variant per call: decode-sized calls
+// (<= 4096 routes) put the weight rows on the MMA M side so each stage carries
+// almost only weight bytes; prefill-sized calls use 128-row x 256-column tiles,
+// whose N=256 MMAs need a third less shared-memory bandwidth per FLOP.
+int resolve_engine(int engine, int64_t num_routes) {
+  if (engine != B200MOE_ENGINE_TCGEN05) return engine;
+  return num_routes <= 4096 ? B200MOE_ENGINE_TCGEN05_SWAP : B200MOE_ENGINE_TCGEN05_WIDE;
+}
 }  // namespace
 }  // namespace b200moe
 
@@ -41,12 +57,18 @@ int b200moe_expert_gate_up(int engine, const void *x, int64_t x_rows, const void
   B200_ARG(w13 && row_route && mtiles && counters && act, "null pointer argument");
   B200_ARG(aligned16(w13) && aligned16(act), "w13 and act must be 16-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  engine = resolve_engine(engine, num_routes);
   if (engine == B200MOE_ENGINE_STREAM) {
     B200_ARG(x != nullptr && aligned16(x), "x must be a 16-byte aligned device pointer");
     return stream_gate_up(x, x_rows, hidden, inter, w13, row_route, token_of_route, top_k,
                           num_routes, mtiles, max_mtiles, counters, act, s);
   }
-  if (engine == B200MOE_ENGINE_TCGEN05) {
+  if (engine == B200MOE_ENGINE_TCGEN05_SWAP) {
+    B200_ARG(x_packed != nullptr && aligned16(x_packed), "x_packed must be 16-byte aligned");
+    return tcs_gate_up(x_packed, hidden, inter, w13, num_local_experts, row_capacity, mtiles,
+                       max_mtiles, counters, act, s);
+  }
+  if (engine == B200MOE_ENGINE_TCGEN05_WIDE) {
     B200_ARG(x_packed != nullptr && aligned16(x_packed), "x_packed must be 16-byte aligned");
     return tc_gate_up(x_packed, hidden, inter, w13, num_local_experts, num_routes, row_capacity,
                       mtiles, max_mtiles, counters, act, s);
@@ -70,10 +92,14 @@ int b200moe_expert_down(int engine, const void *act, int hidden, int inter, cons
            "null pointer argument");
   B200_ARG(aligned16(act) && aligned16(w2) && aligned16(y), "act, w2, y must be 16-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  engine = resolve_engine(engine, num_routes);
   if (engine == B200MOE_ENGINE_STREAM)
     return stream_down(act, hidden, inter, w2, row_route, route_weights, num_routes,
                        max_expert_rows, mtiles, max_mtiles, counters, y, s);
-  if (engine == B200MOE_ENGINE_TCGEN05)
+  if (engine == B200MOE_ENGINE_TCGEN05_SWAP)
+    return tcs_down(act, hidden, inter, w2, num_local_experts, row_route, route_weights,
+                    num_routes, row_capacity, mtiles, max_mtiles, counters, y, s);
+  if (engine == B200MOE_ENGINE_TCGEN05_WIDE)
     return tc_down(act, hidden, inter, w2, num_local_experts, row_route, route_weights,
                    num_routes, row_capacity, mtiles, max_mtiles, counters, y, s);
   set_error("unknown engine %d", engine);

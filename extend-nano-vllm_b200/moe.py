@@ -219,7 +219,8 @@ class ExpertParallelMoE(nn.Module):
         # Kernel entry points; tests may substitute an object with the same
         # functions to exercise the host logic without a GPU.
         self._ops = _native_ops
-        # "auto" | "stream" | "tcgen05": expert GEMM engine selection.
+        # "auto" | "stream" | "tcgen05" | "tcgen05-wide" | "tcgen05-swap": expert
+        # GEMM engine ("tcgen05" lets the library pick the variant per call).
         self.expert_engine = "auto"
         # Optional object with begin(name)/end(name) that records CUDA events
         # around the grouped GEMM launches (used by the benchmark).
@@ -432,6 +433,10 @@ class ExpertParallelMoE(nn.Module):
             return _lib.ENGINE_STREAM
         if self.expert_engine == "tcgen05":
             return _lib.ENGINE_TCGEN05
+        if self.expert_engine == "tcgen05-wide":
+            return _lib.ENGINE_TCGEN05_WIDE
+        if self.expert_engine == "tcgen05-swap":
+            return _lib.ENGINE_TCGEN05_SWAP
         if self.expert_engine != "auto":
             raise ValueError(f"unknown expert engine {self.expert_engine!r}")
         return _lib.ENGINE_STREAM if num_routes <= STREAM_ENGINE_MAX_ROUTES else _lib.ENGINE_TCGEN05
@@ -443,7 +448,7 @@ class ExpertParallelMoE(nn.Module):
         ops = self._ops
         timer = self.kernel_timer
         if engine == _lib.ENGINE_STREAM:
-            x_packed = None
+            x_packed = None  # the streaming engine reads token rows directly
         else:
             x_packed = ops.gather_rows(x, packed, top_k, token_of_route)
         if timer is not None:

@@ -46,7 +46,12 @@ extern "C" {
 
 /* ---- expert GEMM engines ---------------------------------------------------- */
 #define B200MOE_ENGINE_STREAM 0 /* CUDA-core weight streaming (small decode buckets) */
-#define B200MOE_ENGINE_TCGEN05 1 /* tcgen05/TMEM grouped GEMM fed by TMA */
+#define B200MOE_ENGINE_TCGEN05 1 /* tcgen05/TMEM grouped GEMM fed by TMA; the variant is
+                                   chosen per call: SWAP for <= 4096 routes, else WIDE */
+#define B200MOE_ENGINE_TCGEN05_WIDE 2 /* routed rows as the MMA M operand (128-row tiles),
+                                        128/256-wide weight tiles as N */
+#define B200MOE_ENGINE_TCGEN05_SWAP 3 /* weight rows as the MMA M operand (128 features),
+                                        routed rows as N (rounded to 16) */
 
 /* Size of the 128-row work-tile records written by b200moe_pack_routes:
  * {local expert, first packed row, end packed row (exclusive)}. */

@@ -213,21 +213,28 @@ TINY = wl.LayerShape("tiny", 32, 64, 128, 8)
 A = wl.QWEN3_30B_A3B
 
 
-@pytest.mark.parametrize("engine", [_lib.ENGINE_STREAM, _lib.ENGINE_TCGEN05])
+ENGINES = [_lib.ENGINE_STREAM, _lib.ENGINE_TCGEN05, _lib.ENGINE_TCGEN05_WIDE,
+           _lib.ENGINE_TCGEN05_SWAP]
+
+
+@pytest.mark.parametrize("engine", ENGINES)
 @pytest.mark.parametrize("shape,tokens", [(SMALL, 22), (SMALL, 300), (TINY, 16), (TINY, 512),
-                                          (A, 1), (A, 8), (A, 64)])
+                                          (A, 1), (A, 8), (A, 64), (A, 640)])
 def test_expert_engines_match_oracle(engine, shape, tokens):
     _expert_case(shape, tokens, engine, seed=100 + tokens)
 
 
-def test_tcgen05_prefill_with_capacity_matches_oracle():
-    _expert_case(A, 2048, _lib.ENGINE_TCGEN05, seed=7, logits_kind="zipf",
+@pytest.mark.parametrize("engine", [_lib.ENGINE_TCGEN05, _lib.ENGINE_TCGEN05_WIDE,
+                                    _lib.ENGINE_TCGEN05_SWAP])
+def test_tcgen05_prefill_with_capacity_matches_oracle(engine):
+    _expert_case(A, 2048, engine, seed=7, logits_kind="zipf",
                  capacity=wl.capacity_for(2048, A, 1.25))
 
 
 def test_engines_agree_and_are_repeatable():
-    outs = [_expert_case(A, 16, e, seed=3) for e in (_lib.ENGINE_STREAM, _lib.ENGINE_TCGEN05)]
-    assert_close_rel(outs[0].float().cpu().numpy(), outs[1].float().cpu().numpy())
+    outs = [_expert_case(A, 16, e, seed=3) for e in ENGINES]
+    for other in outs[1:]:
+        assert_close_rel(outs[0].float().cpu().numpy(), other.float().cpu().numpy())
     again = _expert_case(A, 16, _lib.ENGINE_TCGEN05, seed=3)
     assert torch.equal(again, outs[1])
 
