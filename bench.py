@@ -67,19 +67,52 @@ def parse_args():
     p.add_argument("--impl", choices=("native", "reference"), default="native")
     p.add_argument("--no-sweep", action="store_true", help="skip the N=1 decode/prefill sweep")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--profile-case", choices=("gemm-small",), default=None,
-                   help="run a small case for ncu captures and exit (no JSON line): "
-                        "gemm-small = 235B-shaped experts, 16 experts x 320 routed rows, "
-                        "604 MB of weights (larger than L2), --steps forwards")
+    p.add_argument("--profile-case", choices=("gemm-small", "decode", "prefill"), default=None,
+                   help="run a case for ncu captures and exit (no JSON line): gemm-small = "
+                        "235B-shaped experts, 16 experts x 320 routed rows, 604 MB of "
+                        "weights (larger than L2), --steps forwards; decode = the 30B-A3B "
+                        "decode bucket of --profile-tokens tokens captured in a CUDA graph "
+                        "and replayed --steps times; prefill = the T=8192 Zipf prefill "
+                        "case, --steps forwards")
+    p.add_argument("--profile-tokens", type=int, default=1)
     return p.parse_args()
 
 
 def profile_case(args) -> None:
-    """Small workload with the headline's per-expert structure, for ncu."""
+    """Small workloads for ncu captures (see --profile-case)."""
     import extend_nano_vllm_b200.workloads as wl
 
     torch.cuda.set_device(0)
     device = torch.device("cuda", 0)
+    if args.profile_case == "decode":
+        shape = wl.QWEN3_30B_A3B
+        layer = build_layer(shape, 1, 0, device, graph_safe_decode=True)
+        t = args.profile_tokens
+        x = wl.hidden_states(t, shape.hidden, seed=300 + t, device=device)
+        logits = wl.uniform_logits(t, shape.num_experts, seed=400 + t, device=device)
+        stream = torch.cuda.Stream()
+        stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(stream):
+            layer._forward_from_logits(x, logits)
+        torch.cuda.current_stream().wait_stream(stream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            layer._forward_from_logits(x, logits)
+        for _ in range(max(1, args.steps)):
+            graph.replay()
+        torch.cuda.synchronize()
+        print(f"profile case decode T={t}: {args.steps} graph replays", flush=True)
+        return
+    if args.profile_case == "prefill":
+        shape = wl.QWEN3_30B_A3B
+        layer = build_layer(shape, 1, 0, device, expert_capacity_factor=1.25)
+        x = wl.hidden_states(PREFILL_TOKENS, shape.hidden, seed=500, device=device)
+        logits = wl.zipf_logits(PREFILL_TOKENS, shape.num_experts, seed=501, device=device)
+        for _ in range(max(1, args.steps)):
+            layer._forward_from_logits(x, logits)
+        torch.cuda.synchronize()
+        print(f"profile case prefill: {args.steps} forwards", flush=True)
+        return
     shape = wl.LayerShape("profile-small", 4096, 1536, 16, 8)
     layer = build_layer(shape, 1, 0, device)
     x = wl.hidden_states(640, shape.hidden, seed=3, device=device)
@@ -107,45 +140,62 @@ def peaks() -> dict:
 # Clocks sampled with nvidia-smi during a timed region.
 # ---------------------------------------------------------------------------
 class ClockSampler:
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """nvidia-smi samples every 50 ms; only those stamped inside [begin, end]
+    of the timed region count (the sampler starts before the region)."""
+
+    QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index: int) -> None:
         self.gpu_index = gpu_index
         self.proc = None
+        self.begin_t = self.end_t = None
 
     def start(self) -> None:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-i", str(self.gpu_index), "-lms", "100"],
+                 "-i", str(self.gpu_index), "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            time.sleep(0.5)  # let the sampler come up before the timed region
         except OSError:
             self.proc = None
+
+    def mark_begin(self) -> None:
+        self.begin_t = datetime.datetime.now()
+
+    def mark_end(self) -> None:
+        self.end_t = datetime.datetime.now()
 
     def stop(self) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.1)
         self.proc.terminate()
         try:
             out, _ = self.proc.communicate(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
             out, _ = self.proc.communicate()
-        rows = [r.split(",") for r in out.strip().splitlines() if r.strip()]
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            r = [c.strip() for c in r]
-            if len(r) < 9:
+        slack = datetime.timedelta(milliseconds=50)
+        for line in out.strip().splitlines():
+            r = [c.strip() for c in line.split(",")]
+            if len(r) < 10:
                 continue
             try:
-                sm.append(float(r[1]))
-                mx.append(float(r[2]))
+                stamp = datetime.datetime.strptime(r[0], "%Y/%m/%d %H:%M:%S.%f")
+                clock, clock_max = float(r[2]), float(r[3])
             except ValueError:
                 continue
-            for name, flag in zip(names, r[5:9]):
+            if self.begin_t and self.end_t and not (
+                    self.begin_t - slack <= stamp <= self.end_t + slack):
+                continue
+            sm.append(clock)
+            mx.append(clock_max)
+            for name, flag in zip(names, r[6:10]):
                 if flag.lower().startswith("active"):
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None,
@@ -400,7 +450,7 @@ def cpu_sample_rate(x_cpu, gate_cpu, w13_cpu, w2_cpu, shape, reps: int) -> tuple
     return x_cpu.size(0) / statistics.median(times), cores
 
 
-def native(args, world, rank, local) -> None:
+def native(args, world, rank, local, json_fd: int = 1) -> None:
     import extend_nano_vllm_b200 as pkg
     import extend_nano_vllm_b200.workloads as wl
     from extend_nano_vllm_b200 import _lib
@@ -421,7 +471,9 @@ def native(args, world, rank, local) -> None:
     layer.kernel_timer = timer
     clocks = ClockSampler(local)
     clocks.start()
+    clocks.mark_begin()
     seconds = time_steps(step, args.steps, 0, world)
+    clocks.mark_end()
     clock_info = clocks.stop()
     layer.kernel_timer = None
     launches = _lib.launches_since(snapshot)
@@ -499,7 +551,8 @@ def native(args, world, rank, local) -> None:
                       "reference CPU algorithm (router + per-expert torch loop, bf16), "
                       "median of 3"}
     if rank == 0:
-        print(json.dumps(record), flush=True)
+        sys.stdout.flush()
+        os.write(json_fd, (json.dumps(record) + "\n").encode())
 
 
 # ---------------------------------------------------------------------------
@@ -558,9 +611,14 @@ def main() -> None:
         rank = int(os.environ.get("RANK", "0"))
         reference(args, int(os.environ.get("WORLD_SIZE", "1")), rank)
         return
+    # Only the JSON line goes to stdout: anything else written to fd 1 while the
+    # benchmark runs (library banners, e.g. NCCL's version line) goes to stderr.
+    sys.stdout.flush()
+    json_fd = os.dup(1)
+    os.dup2(2, 1)
     world, rank, local = init_dist(args)
     try:
-        native(args, world, rank, local)
+        native(args, world, rank, local, json_fd)
     finally:
         if world > 1:
             dist.destroy_process_group()
