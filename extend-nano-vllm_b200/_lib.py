@@ -52,6 +52,8 @@ SIGNATURES: dict[str, tuple] = {
                                     _L, _P, _P, _P]),
     "b200moe_expert_down": (_I, [_I, _P, _I, _I, _P, _I, _P, _P, _L, _L, _L, _P, _L, _P, _P,
                                  _P]),
+    "b200moe_decode_tiny": (_I, [_P, _I, _P, _L, _I, _I, _I, _I, _I, _P, _P, _I, _P, _I, _P, _P,
+                                 _P, _P]),
     "b200moe_combine": (_I, [_P, _L, _P, _L, _I, _I, _I, _P, _I, _P]),
     "b200moe_ep_plan": (_I, [_P, _L, _I, _I, _P, _I, _P, _P, _P, _P]),
     "b200moe_ep_pack": (_I, [_P, _I, _P, _P, _L, _I, _I, _P, _I, _P, _P, _P, _P, _P, _P, _P]),
@@ -88,7 +90,8 @@ LIB = _load()
 
 # Kernels each entry point launches (for launch accounting; the streaming
 # and tcgen05 engines both launch one kernel per projection).
-KERNELS_PER_CALL = {"b200moe_pack_routes": 2, "b200moe_pack_routes_static_scratch": 2}
+KERNELS_PER_CALL = {"b200moe_pack_routes": 2, "b200moe_pack_routes_static_scratch": 2,
+                    "b200moe_decode_tiny": 2}
 # Calls made through call(), by entry-point name (launch accounting).
 CALL_COUNTS: dict[str, int] = {}
 

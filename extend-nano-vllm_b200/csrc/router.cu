@@ -7,9 +7,7 @@
 // Selection ranks experts by descending logit with ties going to the lower
 // index; softmax is monotone so this is the same set and order as top-k over
 // the probabilities wherever the probabilities are distinct.
-#include <float.h>
-
-#include "common.cuh"
+#include "route_warp.cuh"
 
 namespace b200moe {
 namespace {
@@ -23,75 +21,10 @@ __global__ void __launch_bounds__(256) route_topk_kernel(const T *__restrict__ l
   const int lane = threadIdx.x & 31;
   const int64_t token = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   if (token >= num_tokens) return;
-  const T *row = logits + token * num_experts;
-
-  // Element i of this lane is expert lane + 32 * i (coalesced loads).
-  float v[VPT];
-  bool live[VPT];
-#pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    const int e = lane + 32 * i;
-    live[i] = e < num_experts;
-    v[i] = live[i] ? to_f32(row[e]) : -FLT_MAX;
-  }
-  float m = -INFINITY;
-#pragma unroll
-  for (int i = 0; i < VPT; ++i)
-    if (live[i]) m = fmaxf(m, v[i]);
-  m = warp_max(m);
-  float p[VPT];
-  float s = 0.f;
-#pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    p[i] = live[i] ? expf(v[i] - m) : 0.f;
-    s += p[i];
-  }
-  s = warp_sum(s);
-#pragma unroll
-  for (int i = 0; i < VPT; ++i) p[i] = p[i] / s;
-
-  // k rounds of warp arg-max over (logit desc, index asc).
-  float my_w = 0.f;
-  int my_id = 0;
-  for (int slot = 0; slot < top_k; ++slot) {
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
-    float bp = 0.f;
-#pragma unroll
-    for (int i = 0; i < VPT; ++i) {
-      const int e = lane + 32 * i;
-      if (live[i] && (v[i] > bv || (v[i] == bv && e < bi))) {
-        bv = v[i];
-        bi = e;
-        bp = p[i];
-      }
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-      const float op = __shfl_xor_sync(0xffffffffu, bp, off);
-      if (ov > bv || (ov == bv && oi < bi)) {
-        bv = ov;
-        bi = oi;
-        bp = op;
-      }
-    }
-    // The owning lane retires the winner.
-#pragma unroll
-    for (int i = 0; i < VPT; ++i)
-      if (lane + 32 * i == bi) live[i] = false;
-    if (lane == slot) {
-      my_w = bp;
-      my_id = bi;
-    }
-  }
-  if (renormalize) {
-    // Sequential sum over the slots, identical on every lane.
-    float total = 0.f;
-    for (int slot = 0; slot < top_k; ++slot) total += __shfl_sync(0xffffffffu, my_w, slot);
-    my_w = my_w / total;
-  }
+  float my_w;
+  int my_id;
+  warp_route_token<T, VPT>(logits + token * num_experts, num_experts, top_k, renormalize, lane,
+                           &my_w, &my_id);
   if (lane < top_k) {
     weights[token * top_k + lane] = __float2bfloat16_rn(my_w);
     ids[token * top_k + lane] = my_id;

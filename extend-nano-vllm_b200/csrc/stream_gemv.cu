@@ -17,7 +17,8 @@
 //    half, for long rows) before reducing.
 //  * Results go through shared memory and leave as one 16-byte store per
 //    route and warp.
-#include "common.cuh"
+#include "route_warp.cuh"
+#include "stream_common.cuh"
 
 namespace b200moe {
 namespace {
@@ -26,47 +27,6 @@ constexpr int kStreamThreads = 128;  // 4 warps
 constexpr int kStreamWarps = kStreamThreads / 32;
 constexpr int kFeatPerWarp = 8;      // outputs per warp (one 16B store per route)
 constexpr int kRows = 8;             // routes per shared-memory chunk
-
-__device__ __forceinline__ uint4 ld_stream(const uint4 *p) {
-  uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
-}
-
-__device__ __forceinline__ void store8_bf16(__nv_bfloat16 *dst, const float *v) {
-  uint4 o;
-  __nv_bfloat162 *op = reinterpret_cast<__nv_bfloat162 *>(&o);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) op[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
-  *reinterpret_cast<uint4 *>(dst) = o;
-}
-
-template <int VPL>
-__device__ __forceinline__ void load_row(const uint4 *row, int V, int lane, uint4 (&w)[VPL]) {
-#pragma unroll
-  for (int i = 0; i < VPL; ++i) {
-    const int v = lane + 32 * i;
-    w[i] = v < V ? ld_stream(row + v) : make_uint4(0, 0, 0, 0);
-  }
-}
-
-// Dot products of one weight row with NR activation rows held in shared memory.
-template <int VPL, int NR>
-__device__ __forceinline__ void dot_rows(const uint4 (&w)[VPL], const uint4 *xs, int V, int lane,
-                                         float (&acc)[NR]) {
-#pragma unroll
-  for (int n = 0; n < NR; ++n) acc[n] = 0.f;
-#pragma unroll
-  for (int i = 0; i < VPL; ++i) {
-    const int v = lane + 32 * i;
-    if (v < V) {
-#pragma unroll
-      for (int n = 0; n < NR; ++n) dot8_bf16(w[i], xs[n * V + v], acc[n]);
-    }
-  }
-}
 
 // One chunk of NR routes for the warp's 8 features; results to res[f][n].
 template <int VPL, int NR>
@@ -308,6 +268,218 @@ int launch_down_stream(dim3 grid, size_t smem, cudaStream_t s, const __nv_bfloat
   return B200MOE_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Fused tiny-batch decode (at most 16 routes, no capacity): two launches
+// replace router + packing + two projections + combine.  Every CTA routes its
+// own token with the router's warp routine, so no packing is needed; the
+// arithmetic (routing, gate/up rows, down rows, bf16 rounding points, fp32
+// slot-order sum) is the same as the unfused streaming path, so the results
+// are identical to it.
+// ---------------------------------------------------------------------------
+constexpr int kTinyWarps = 8;       // gate/up: 8 warps x 4 features per CTA
+constexpr int kTinyFeat = 4;
+constexpr int kTinyDownRows = 8;    // down: 8 output rows per CTA, one warp per route slot
+
+__device__ __forceinline__ int local_expert(int e, int num_experts, const int64_t *local_index,
+                                            int expert_start, int num_local) {
+  if (e < 0 || e >= num_experts) return -1;
+  if (local_index) {
+    const int64_t l = local_index[e];
+    return (l >= 0 && l < num_local) ? static_cast<int>(l) : -1;
+  }
+  return (e >= expert_start && e < expert_start + num_local) ? e - expert_start : -1;
+}
+
+// grid = (num_tokens * top_k, ceil(I / 32)); block = 256.  act: [T*k, I].
+// Warp w owns features j0..j0+3 and streams their gate/up rows with one row
+// in flight ahead; the dot products and SwiGLU are those of gate_up_chunk.
+template <typename TL, int VPT, int VPL>
+__global__ void __launch_bounds__(32 * kTinyWarps) tiny_gate_up_kernel(
+    const TL *__restrict__ logits, const __nv_bfloat16 *__restrict__ x, int hidden, int inter,
+    int num_experts, int top_k, int renormalize, const __nv_bfloat16 *__restrict__ w13,
+    int num_local, const int64_t *__restrict__ local_index, int expert_start,
+    __nv_bfloat16 *__restrict__ act, int64_t *__restrict__ stats) {
+  extern __shared__ uint4 xs[];  // [V]
+  __shared__ int s_expert;
+  const int route = blockIdx.x;
+  const int token = route / top_k;
+  const int slot = route - token * top_k;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int V = hidden / 8;
+  if (warp == 0) {
+    float w;
+    int id;
+    warp_route_token<TL, VPT>(logits + static_cast<int64_t>(token) * num_experts, num_experts,
+                              top_k, renormalize, lane, &w, &id);
+    if (lane == slot) s_expert = id;
+  }
+  const uint4 *xrow = reinterpret_cast<const uint4 *>(x + static_cast<int64_t>(token) * hidden);
+  for (int v = threadIdx.x; v < V; v += blockDim.x) xs[v] = xrow[v];
+  __syncthreads();
+  const int le = local_expert(s_expert, num_experts, local_index, expert_start, num_local);
+  if (le < 0) return;
+  if (stats && blockIdx.y == 0 && threadIdx.x == 0)
+    atomicAdd(reinterpret_cast<unsigned long long *>(&stats[0]), 1ull);
+  const int j0 = (blockIdx.y * kTinyWarps + warp) * kTinyFeat;
+  if (j0 >= inter) return;
+  const int nfeat = min(kTinyFeat, inter - j0);
+  const __nv_bfloat16 *w_exp = w13 + static_cast<int64_t>(le) * 2 * inter * hidden;
+  auto row_ptr = [&](int s) {
+    const int j = j0 + (s >> 1);
+    const int row = (s & 1) ? inter + j : j;
+    return reinterpret_cast<const uint4 *>(w_exp + static_cast<int64_t>(row) * hidden);
+  };
+  float res[kTinyFeat] = {0.f, 0.f, 0.f, 0.f};
+  uint4 cur[VPL];
+  load_row<VPL>(row_ptr(0), V, lane, cur);
+  float gsum = 0.f;
+#pragma unroll
+  for (int s = 0; s < 2 * kTinyFeat; ++s) {
+    if ((s >> 1) >= nfeat) break;
+    uint4 nxt[VPL];
+    const bool more = s + 1 < 2 * nfeat;
+    if (more) load_row<VPL>(row_ptr(s + 1), V, lane, nxt);
+    float acc[1];
+    dot_rows<VPL, 1>(cur, xs, V, lane, acc);
+    const float sum = warp_sum(acc[0]);
+    if ((s & 1) == 0)
+      gsum = sum;
+    else
+      res[s >> 1] = swiglu_bf16(gsum, sum);
+    if (more) {
+#pragma unroll
+      for (int i = 0; i < VPL; ++i) cur[i] = nxt[i];
+    }
+  }
+  if (lane == 0) {
+    __nv_bfloat16 *dst = act + static_cast<int64_t>(route) * inter + j0;
+    for (int f = 0; f < nfeat; ++f) dst[f] = __float2bfloat16_rn(res[f]);
+  }
+}
+
+// grid = (num_tokens, ceil(H / 8)); block = 32 * top_k.  Warp s computes the
+// bf16 down-projection rows of route slot s for the CTA's 8 outputs; the
+// routes are then summed in fp32 in slot order and stored as bf16.
+template <typename TL, int VPT, int VPL>
+__global__ void __launch_bounds__(512) tiny_down_combine_kernel(
+    const TL *__restrict__ logits, const __nv_bfloat16 *__restrict__ act, int hidden, int inter,
+    int num_experts, int top_k, int renormalize, const __nv_bfloat16 *__restrict__ w2,
+    int num_local, const int64_t *__restrict__ local_index, int expert_start,
+    __nv_bfloat16 *__restrict__ out) {
+  constexpr int RB = VPL <= 3 ? 8 : 4;  // rows in flight per warp
+  extern __shared__ uint4 as[];  // [top_k][V]
+  __shared__ int s_le[16];
+  __shared__ float s_w[16];
+  __shared__ float s_y[16][kTinyDownRows];
+  const int token = blockIdx.x;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int V = inter / 8;
+  if (warp == 0) {
+    float w;
+    int id;
+    warp_route_token<TL, VPT>(logits + static_cast<int64_t>(token) * num_experts, num_experts,
+                              top_k, renormalize, lane, &w, &id);
+    if (lane < top_k) {
+      s_le[lane] = local_expert(id, num_experts, local_index, expert_start, num_local);
+      s_w[lane] = bf16_round(w);  // the router stores bf16 weights
+    }
+  }
+  __syncthreads();
+  const int le = s_le[warp];
+  if (le >= 0) {
+    const uint4 *src = reinterpret_cast<const uint4 *>(
+        act + (static_cast<int64_t>(token) * top_k + warp) * inter);
+    for (int v = lane; v < V; v += 32) as[warp * V + v] = src[v];
+  }
+  __syncwarp();
+  const int h0 = blockIdx.y * kTinyDownRows;
+  if (le >= 0) {
+    const __nv_bfloat16 *w_exp = w2 + static_cast<int64_t>(le) * hidden * inter;
+#pragma unroll
+    for (int f0 = 0; f0 < kTinyDownRows; f0 += RB) {
+      uint4 w[RB][VPL];
+#pragma unroll
+      for (int r = 0; r < RB; ++r) {
+        const int h = h0 + f0 + r;
+        if (h < hidden)
+          load_row<VPL>(reinterpret_cast<const uint4 *>(w_exp + static_cast<int64_t>(h) * inter),
+                        V, lane, w[r]);
+      }
+#pragma unroll
+      for (int r = 0; r < RB; ++r) {
+        if (h0 + f0 + r < hidden) {
+          float acc[1];
+          dot_rows<VPL, 1>(w[r], as + warp * V, V, lane, acc);
+          const float y = bf16_round(warp_sum(acc[0]) * s_w[warp]);
+          if (lane == 0) s_y[warp][f0 + r] = y;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < kTinyDownRows && h0 + static_cast<int>(threadIdx.x) < hidden) {
+    float total = 0.f;
+    for (int s = 0; s < top_k; ++s)
+      if (s_le[s] >= 0) total += s_y[s][threadIdx.x];
+    out[static_cast<int64_t>(token) * hidden + h0 + threadIdx.x] = __float2bfloat16_rn(total);
+  }
+}
+
+template <typename TL, int VPT, int VPLG, int VPLD>
+int launch_tiny(const void *logits, const void *x, int64_t num_tokens, int hidden, int inter,
+                int num_experts, int top_k, int renormalize, const void *w13, const void *w2,
+                int num_local, const int64_t *local_index, int expert_start, void *act, void *out,
+                int64_t *stats, cudaStream_t s) {
+  const auto *lg = static_cast<const TL *>(logits);
+  const dim3 g1(static_cast<unsigned>(num_tokens * top_k),
+                static_cast<unsigned>((inter + kTinyWarps * kTinyFeat - 1) /
+                                      (kTinyWarps * kTinyFeat)));
+  const size_t smem1 = static_cast<size_t>(hidden / 8) * sizeof(uint4);
+  if (smem1 > 48 * 1024)
+    B200_CUDA(cudaFuncSetAttribute(tiny_gate_up_kernel<TL, VPT, VPLG>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1));
+  tiny_gate_up_kernel<TL, VPT, VPLG><<<g1, 32 * kTinyWarps, smem1, s>>>(
+      lg, static_cast<const __nv_bfloat16 *>(x), hidden, inter, num_experts, top_k, renormalize,
+      static_cast<const __nv_bfloat16 *>(w13), num_local, local_index, expert_start,
+      static_cast<__nv_bfloat16 *>(act), stats);
+  B200_LAUNCHED();
+  const dim3 g2(static_cast<unsigned>(num_tokens),
+                static_cast<unsigned>((hidden + kTinyDownRows - 1) / kTinyDownRows));
+  const size_t smem2 = static_cast<size_t>(top_k) * (inter / 8) * sizeof(uint4);
+  if (smem2 > 48 * 1024)
+    B200_CUDA(cudaFuncSetAttribute(tiny_down_combine_kernel<TL, VPT, VPLD>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2));
+  tiny_down_combine_kernel<TL, VPT, VPLD><<<g2, 32 * top_k, smem2, s>>>(
+      lg, static_cast<const __nv_bfloat16 *>(act), hidden, inter, num_experts, top_k,
+      renormalize, static_cast<const __nv_bfloat16 *>(w2), num_local, local_index, expert_start,
+      static_cast<__nv_bfloat16 *>(out));
+  B200_LAUNCHED();
+  return B200MOE_OK;
+}
+
+template <typename TL, int VPT>
+int dispatch_tiny(const void *logits, const void *x, int64_t num_tokens, int hidden, int inter,
+                  int num_experts, int top_k, int renormalize, const void *w13, const void *w2,
+                  int num_local, const int64_t *local_index, int expert_start, void *act,
+                  void *out, int64_t *stats, cudaStream_t s) {
+  const int vg = (hidden / 8 + 31) / 32;
+  const int vd = (inter / 8 + 31) / 32;
+#define B200_TINY(G, D)                                                                         \
+  if (vg <= G && vd <= D)                                                                       \
+    return launch_tiny<TL, VPT, G, D>(logits, x, num_tokens, hidden, inter, num_experts, top_k, \
+                                      renormalize, w13, w2, num_local, local_index,             \
+                                      expert_start, act, out, stats, s);
+  B200_TINY(1, 1)
+  B200_TINY(8, 3)
+  B200_TINY(16, 6)
+  B200_TINY(16, 8)
+#undef B200_TINY
+  set_error("tiny decode path: hidden %d / intermediate %d unsupported", hidden, inter);
+  return B200MOE_EUNSUPPORTED;
+}
+
 }  // namespace
 
 int nr_bound(int64_t max_expert_rows) {
@@ -382,3 +554,39 @@ int stream_down(const void *act, int hidden, int inter, const void *w2, const in
 }
 
 }  // namespace b200moe
+
+extern "C" int b200moe_decode_tiny(const void *logits, int logits_dtype, const void *x,
+                                   int64_t num_tokens, int hidden, int inter, int num_experts,
+                                   int top_k, int renormalize, const void *w13, const void *w2,
+                                   int num_local_experts, const int64_t *local_index,
+                                   int expert_start, void *act, void *out, int64_t *stats,
+                                   void *stream) {
+  using namespace b200moe;
+  B200_ARG(num_tokens >= 0 && hidden > 0 && inter > 0 && num_local_experts > 0, "bad shape");
+  B200_ARG(top_k >= 1 && top_k <= num_experts, "top_k must be between 1 and num_experts");
+  B200_UNSUPPORTED(num_tokens * top_k <= 16, "the tiny decode path takes at most 16 routes");
+  B200_UNSUPPORTED(num_experts <= 1024, "num_experts %d > 1024 is not supported", num_experts);
+  B200_UNSUPPORTED(hidden % 16 == 0 && inter % 16 == 0 && hidden <= 4096 && inter <= 2048,
+                   "hidden/intermediate sizes must be multiples of 16 (max 4096/2048)");
+  if (num_tokens == 0) return B200MOE_OK;
+  B200_ARG(logits && x && w13 && w2 && act && out, "null pointer argument");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int vpt = (num_experts + 31) / 32;
+#define B200_TINY_L(TL, V)                                                                       \
+  if (vpt <= V)                                                                                  \
+    return dispatch_tiny<TL, V>(logits, x, num_tokens, hidden, inter, num_experts, top_k,       \
+                                renormalize, w13, w2, num_local_experts, local_index,           \
+                                expert_start, act, out, stats, s);
+  if (logits_dtype == B200MOE_F32) {
+    B200_TINY_L(float, 1)
+    B200_TINY_L(float, 4)
+    B200_TINY_L(float, 32)
+  } else if (logits_dtype == B200MOE_BF16) {
+    B200_TINY_L(__nv_bfloat16, 1)
+    B200_TINY_L(__nv_bfloat16, 4)
+    B200_TINY_L(__nv_bfloat16, 32)
+  }
+#undef B200_TINY_L
+  set_error("tiny decode path: unsupported logits dtype %d", logits_dtype);
+  return B200MOE_EINVAL;
+}

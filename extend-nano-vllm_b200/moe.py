@@ -428,6 +428,14 @@ class ExpertParallelMoE(nn.Module):
             local_index=local_index, expert_start=max(self.expert_start, 0),
             expert_base=expert_base, capacity=capacity, stats=stats)
 
+    def _use_tiny_path(self, num_tokens: int, logits: torch.Tensor) -> bool:
+        """Two-launch fused path: tiny buckets, no capacity, plain bf16 combine."""
+        return (self.expert_engine == "auto" and self._ops is _native_ops
+                and num_tokens * self.top_k <= _native_ops.TINY_MAX_ROUTES
+                and self.expert_capacity is None and self.expert_capacity_factor is None
+                and not self.fp64_combine and not self.fp32_reduce
+                and logits.dtype in (torch.float32, torch.bfloat16))
+
     def _engine(self, num_routes: int) -> int:
         if self.expert_engine == "stream":
             return _lib.ENGINE_STREAM
@@ -544,6 +552,14 @@ class ExpertParallelMoE(nn.Module):
             return torch.zeros_like(x)
         self._check_inputs(x)
         stats = self._device_stats(x.device)
+        if self._use_tiny_path(num_tokens, logits):
+            local_index = (self.expert_local_index_tensor if self.expert_id_to_local is not None
+                           else None)
+            self.total_assignment_count += num_tokens * self.top_k
+            return self._ops.decode_tiny(
+                logits, x.contiguous(), self.gate_up_proj, self.down_proj, self.top_k,
+                self.norm_topk_prob, self.num_experts, local_index=local_index,
+                expert_start=max(self.expert_start, 0), stats=stats)
         weights, ids = self._ops.route_topk(logits, self.top_k, self.norm_topk_prob)
         flat_w = weights.view(-1)
         packed = self._pack(ids.view(-1), flat_w, capacity=self._capacity(num_tokens),

@@ -169,6 +169,29 @@ def expert_down(engine: int, act: torch.Tensor, w2: torch.Tensor, packed: Packed
     return y
 
 
+TINY_MAX_ROUTES = 16
+
+
+def decode_tiny(logits: torch.Tensor, x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor,
+                top_k: int, renormalize: bool, num_experts: int, *,
+                local_index: torch.Tensor | None = None, expert_start: int = 0,
+                stats: torch.Tensor | None = None) -> torch.Tensor:
+    """Whole expert path for <= 16 routes (no capacity) in two launches -> out [T, H]."""
+    _require_cuda(logits, x)
+    logits = logits.contiguous()
+    if logits.dtype not in (torch.float32, torch.bfloat16):
+        raise TypeError("tiny decode path takes fp32 or bf16 logits")
+    tokens, hidden = x.shape
+    num_local, two_inter, _ = w13.shape
+    inter = two_inter // 2
+    act = torch.empty((tokens * top_k, inter), device=x.device, dtype=torch.bfloat16)
+    out = torch.empty((tokens, hidden), device=x.device, dtype=torch.bfloat16)
+    call("b200moe_decode_tiny", _p(logits), _DTYPE_CODES[logits.dtype], _p(x), tokens, hidden,
+         inter, num_experts, top_k, int(bool(renormalize)), _p(w13), _p(w2), num_local,
+         _p(local_index), int(expert_start), _p(act), _p(out), _p(stats), _stream(x))
+    return out
+
+
 def combine(y: torch.Tensor, route_rows: torch.Tensor | None, num_tokens: int, top_k: int,
             out_dtype: torch.dtype = torch.bfloat16, accum_f64: bool = False) -> torch.Tensor:
     """out[t] = sum_s y[route_rows[t*k+s]] in slot order (rows >= len(y) are zero)."""

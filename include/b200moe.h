@@ -234,6 +234,27 @@ B200MOE_API int b200moe_expert_down(int engine, const void *act, int hidden, int
                         void *y, void *stream);
 
 /*
+ * Fused expert path for tiny decode batches (num_tokens * top_k <= 16, no
+ * capacity limit): router + gate/up + SwiGLU + down + route-order combine in
+ * two launches.  Every CTA routes its token itself (same routine as
+ * b200moe_route_topk), so no packing step is needed; the arithmetic equals the
+ * streaming engine followed by b200moe_combine (bf16 act, bf16 route rows,
+ * fp32 slot-order sum), so results are identical to that path.  Replaces the
+ * reference's whole _forward_static_decode for such buckets
+ * (nanovllm/layers/moe.py:783-868 with _route, :870-878).
+ *   logits [T, E] (BF16/F32), x [T, H] bf16, w13/w2 as above,
+ *   act    [T*top_k, I] bf16 caller scratch,
+ *   out    [T, H] bf16 (routes to non-local experts contribute zero),
+ *   stats  [2] int64 or NULL: stats[0] += local routes.
+ */
+B200MOE_API int b200moe_decode_tiny(const void *logits, int logits_dtype, const void *x,
+                                    int64_t num_tokens, int hidden, int inter, int num_experts,
+                                    int top_k, int renormalize, const void *w13, const void *w2,
+                                    int num_local_experts, const int64_t *local_index,
+                                    int expert_start, void *act, void *out, int64_t *stats,
+                                    void *stream);
+
+/*
  * Route-order combine: out[t, :] = sum_{s < top_k} Y[route_rows[t*top_k+s], :]
  * accumulated in fp32 (accum_f64 != 0: fp64) in slot order, rows >= num_rows
  * read as zero, stored as out_dtype (BF16/F32/F64).  route_rows NULL means the

@@ -236,3 +236,54 @@ def test_relocate_experts_single_rank_keeps_storage():
     assert layer.relocate_experts(tuple(range(1)) * 8) == 0
     assert layer.gate_up_proj.data_ptr() == ptr
     assert torch.equal(layer(x), before)
+
+
+@pytest.mark.parametrize("tokens", [1, 2])
+@pytest.mark.parametrize("placement", ["full", "shard", "round_robin"])
+@torch.inference_mode()
+def test_tiny_decode_path_matches_unfused_streaming_path(tokens, placement):
+    kw = {"full": {}, "shard": dict(ep_rank=1, ep_size=2),
+          "round_robin": dict(ep_rank=1, ep_size=2,
+                              expert_owners=tuple(e % 2 for e in range(128)))}[placement]
+    layer = ExpertParallelMoE(A.hidden, A.intermediate, A.num_experts, A.top_k, True,
+                              **kw).to(device=DEV, dtype=torch.bfloat16)
+    w13, w2 = wl.expert_weights(A, seed=61, device=DEV, on_device=True)
+    local = list(layer.local_expert_ids)
+    with torch.no_grad():
+        layer.gate.weight.copy_(wl.gate_weight(A, seed=62).to(DEV))
+        layer.gate_up_proj.copy_(w13[local])
+        layer.down_proj.copy_(w2[local])
+    x = wl.hidden_states(tokens, A.hidden, seed=63).to(DEV)
+    for logits in (layer.gate(x), wl.uniform_logits(tokens, 128, seed=64).to(DEV)):
+        calls = dict(_lib.CALL_COUNTS)
+        fused = layer._forward_from_logits(x, logits)
+        assert _lib.CALL_COUNTS.get("b200moe_decode_tiny", 0) == calls.get(
+            "b200moe_decode_tiny", 0) + 1
+        layer.expert_engine = "stream"
+        unfused = layer._forward_from_logits(x, logits)
+        layer.expert_engine = "auto"
+        assert torch.equal(fused, unfused)
+    routes = tokens * A.top_k
+    assert layer.dispatch_assignment_count <= 4 * routes
+
+
+@torch.inference_mode()
+def test_tiny_decode_path_graph_replay():
+    layer, *_ = make_layer(SMALL, 71, graph_safe_decode=True)
+    hidden = wl.hidden_states(2, 128, seed=1).to(DEV)
+    second = wl.hidden_states(2, 128, seed=2).to(DEV)
+    expected_first, expected_second = layer(hidden.clone()), layer(second)
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        layer(hidden)
+    torch.cuda.current_stream().wait_stream(stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        output = layer(hidden)
+    hidden.copy_(second)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(output, expected_second)
+    layer.expert_engine = "stream"
+    assert torch.equal(layer(second), expected_second)
