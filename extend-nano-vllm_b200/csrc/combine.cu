@@ -53,11 +53,13 @@ __device__ __forceinline__ void store8<double, double>(double *dst, const double
 
 // One thread per 8 columns of one token.  hidden % 8 == 0.
 template <typename Acc, typename Out>
-__global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16 *__restrict__ y,
+__global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16 *y,
                                                       int64_t num_rows,
-                                                      const int32_t *__restrict__ route_rows,
+                                                      const int32_t *route_rows,
                                                       int64_t num_tokens, int top_k, int hidden,
                                                       Out *__restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int vec_per_row = hidden / 8;
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t token = idx / vec_per_row;
@@ -93,15 +95,15 @@ int launch_combine(const void *y, int64_t num_rows, const int32_t *route_rows,
   const auto *yp = static_cast<const __nv_bfloat16 *>(y);
   switch (out_dtype) {
     case B200MOE_BF16:
-      combine_kernel<Acc, __nv_bfloat16><<<blocks, threads, 0, s>>>(
+      B200_LAUNCH_PDL(kPdlCombine, combine_kernel<Acc, __nv_bfloat16>, dim3(blocks), dim3(threads), 0, s,
           yp, num_rows, route_rows, num_tokens, top_k, hidden, static_cast<__nv_bfloat16 *>(out));
       break;
     case B200MOE_F32:
-      combine_kernel<Acc, float><<<blocks, threads, 0, s>>>(yp, num_rows, route_rows, num_tokens,
+      B200_LAUNCH_PDL(kPdlCombine, combine_kernel<Acc, float>, dim3(blocks), dim3(threads), 0, s, yp, num_rows, route_rows, num_tokens,
                                                             top_k, hidden, static_cast<float *>(out));
       break;
     case B200MOE_F64:
-      combine_kernel<Acc, double><<<blocks, threads, 0, s>>>(
+      B200_LAUNCH_PDL(kPdlCombine, combine_kernel<Acc, double>, dim3(blocks), dim3(threads), 0, s,
           yp, num_rows, route_rows, num_tokens, top_k, hidden, static_cast<double *>(out));
       break;
     default:
@@ -114,10 +116,12 @@ int launch_combine(const void *y, int64_t num_rows, const int32_t *route_rows,
 
 // One warp per packed row; copies hidden bf16 values with 16-byte vectors.
 __global__ void __launch_bounds__(256) gather_rows_kernel(
-    const __nv_bfloat16 *__restrict__ x, int64_t x_rows, int hidden,
-    const int32_t *__restrict__ row_route, const int32_t *__restrict__ token_of_route, int top_k,
-    int64_t num_routes, int64_t row_capacity, const int32_t *__restrict__ counters,
+    const __nv_bfloat16 *x, int64_t x_rows, int hidden, const int32_t *row_route,
+    const int32_t *token_of_route, int top_k, int64_t num_routes, int64_t row_capacity,
+    const int32_t *counters,
     __nv_bfloat16 *__restrict__ x_packed) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t total = counters[B200MOE_CNT_PADDED_ROWS];
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
@@ -170,7 +174,7 @@ int b200moe_gather_rows(const void *x, int64_t x_rows, int hidden, const int32_t
   int64_t blocks = (row_capacity + 7) / 8;
   const int64_t cap = 8LL * b200moe::sm_count();
   if (blocks > cap) blocks = cap;
-  b200moe::gather_rows_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(
+  B200_LAUNCH_PDL(b200moe::kPdlGather, b200moe::gather_rows_kernel, dim3(static_cast<int>(blocks)), dim3(256), 0, s,
       static_cast<const __nv_bfloat16 *>(x), x_rows, hidden, row_route, token_of_route, top_k,
       num_routes, row_capacity, counters, static_cast<__nv_bfloat16 *>(x_packed));
   B200_LAUNCHED();

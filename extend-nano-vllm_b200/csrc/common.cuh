@@ -16,6 +16,19 @@ namespace b200moe {
 void set_error(const char *fmt, ...);
 int sm_count();                    // SMs of the current device
 int current_device();
+// Kernel families whose launches use programmatic dependent launch; the
+// B200MOE_PDL environment variable (read once) holds the enabled mask,
+// default all.  "0" turns programmatic launch off everywhere.
+enum PdlFamily : unsigned {
+  kPdlRoute = 1u,
+  kPdlPack = 2u,
+  kPdlGather = 4u,
+  kPdlCombine = 8u,
+  kPdlStream = 16u,
+  kPdlTiny = 32u,
+  kPdlTcgen05 = 64u,
+};
+bool pdl_enabled(unsigned family);
 // Device-side sticky status word (bit 0: bounded wait gave up, bit 1: index
 // out of range).  Kernels OR bits into it; the host reads it through
 // b200moe_device_status.
@@ -51,8 +64,35 @@ constexpr int kStatusIndex = 2;
   } while (0)
 
 #define B200_LAUNCHED() B200_CUDA(cudaGetLastError())
+#define B200_LAUNCH_PDL(...) B200_CUDA(b200moe::launch_pdl(__VA_ARGS__))
 
 namespace b200moe {
+
+// Programmatic dependent launch: every hot-path kernel lets the next kernel in
+// its stream start launching at once (pdl_trigger) and waits for the previous
+// kernel's results (pdl_wait) before reading them, so launches and prologues
+// overlap the tail of the predecessor.  Both are no-ops when the kernel was
+// launched without the programmatic-serialization attribute.
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(unsigned family, void (*kernel)(KArgs...), dim3 grid, dim3 block,
+                       size_t smem, cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled(family) ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
 
 __host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
 __host__ __device__ __forceinline__ int64_t max64(int64_t a, int64_t b) { return a > b ? a : b; }

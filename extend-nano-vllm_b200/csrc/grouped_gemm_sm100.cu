@@ -95,9 +95,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int num_mtiles =
-      static_cast<int>(min64(args.counters[B200MOE_CNT_MTILES], args.max_mtiles));
-  const int num_work = num_mtiles * args.n_tiles;
+  pdl_trigger();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -123,6 +121,12 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  // The prologue above overlaps the previous kernel; the m-tile list and the
+  // operands are its outputs.
+  pdl_wait();
+  const int num_mtiles =
+      static_cast<int>(min64(args.counters[B200MOE_CNT_MTILES], args.max_mtiles));
+  const int num_work = num_mtiles * args.n_tiles;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -338,7 +342,8 @@ int launch(const CUtensorMap &ma, const CUtensorMap &mb, const Args &args, cudaS
   int grid = sm_count();
   if (work < grid) grid = static_cast<int>(work);
   if (grid < 1) grid = 1;
-  grouped_gemm_kernel<kGateUp, BN><<<grid, THREADS, Cfg<BN>::SMEM_BYTES, s>>>(ma, mb, args);
+  B200_LAUNCH_PDL(kPdlTcgen05, grouped_gemm_kernel<kGateUp, BN>, dim3(grid), dim3(THREADS), Cfg<BN>::SMEM_BYTES, s,
+                  ma, mb, args);
   B200_LAUNCHED();
   return B200MOE_OK;
 }

@@ -53,9 +53,11 @@ __device__ __forceinline__ int route_key(int64_t id, int num_experts) {
 }
 
 __global__ void __launch_bounds__(kPackThreads) pack_hist_kernel(
-    const int64_t *__restrict__ ids, int64_t num_routes, int num_experts, int64_t chunk,
+    const int64_t *ids, int64_t num_routes, int num_experts, int64_t chunk,
     int32_t *__restrict__ hist, int32_t *__restrict__ row_route, int64_t row_capacity,
     int32_t *__restrict__ tile_expert, int32_t *__restrict__ counters) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ int32_t sh_hist[];
   const int E1 = num_experts + 1;
   for (int e = threadIdx.x; e < E1; e += blockDim.x) sh_hist[e] = 0;
@@ -104,6 +106,8 @@ struct ScatterArgs {
 // Shared memory (int32 words): base[E1] tot[E1] run[E1] loc[E1]
 // warp_cnt[8][E1] lstart[L] lkept[L] gof[L] mstart[L] + 4 reduction words.
 __global__ void __launch_bounds__(kPackThreads) pack_scatter_kernel(ScatterArgs a) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ int32_t sm[];
   const int E = a.num_experts;
   const int E1 = E + 1;
@@ -378,7 +382,7 @@ int b200moe_pack_routes(int64_t *expert_ids, void *route_weights, int64_t num_ro
   int32_t *hist = static_cast<int32_t *>(scratch);
 
   const size_t hist_smem = sizeof(int32_t) * (num_experts + 1);
-  pack_hist_kernel<<<g.nblk, kPackThreads, hist_smem, s>>>(
+  B200_LAUNCH_PDL(kPdlPack, pack_hist_kernel, dim3(g.nblk), dim3(kPackThreads), hist_smem, s,
       expert_ids, num_routes, num_experts, g.chunk, hist, row_route, row_capacity, tile_expert,
       counters);
   B200_LAUNCHED();
@@ -412,7 +416,7 @@ int b200moe_pack_routes(int64_t *expert_ids, void *route_weights, int64_t num_ro
     B200_CUDA(cudaFuncSetAttribute(pack_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    static_cast<int>(smem)));
   }
-  pack_scatter_kernel<<<g.nblk, kPackThreads, smem, s>>>(a);
+  B200_LAUNCH_PDL(kPdlPack, pack_scatter_kernel, dim3(g.nblk), dim3(kPackThreads), smem, s, a);
   B200_LAUNCHED();
   return B200MOE_OK;
 }

@@ -15,7 +15,7 @@ namespace b200moe {
 // if requested, fp32, not yet rounded) in *w and its expert id in *id.
 // VPL = ceil(num_experts / 32) logits per lane (expert lane + 32 * i).
 template <typename T, int VPL>
-__device__ __forceinline__ void warp_route_token(const T *__restrict__ row, int num_experts,
+__device__ __forceinline__ void warp_route_token(const T *row, int num_experts,
                                                  int top_k, int renormalize, int lane,
                                                  float *w, int *id) {
   float v[VPL];

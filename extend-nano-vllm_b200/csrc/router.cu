@@ -13,11 +13,13 @@ namespace b200moe {
 namespace {
 
 template <typename T, int VPT>
-__global__ void __launch_bounds__(256) route_topk_kernel(const T *__restrict__ logits,
+__global__ void __launch_bounds__(256) route_topk_kernel(const T *logits,
                                                          int64_t num_tokens, int num_experts,
                                                          int top_k, int renormalize,
                                                          __nv_bfloat16 *__restrict__ weights,
                                                          int64_t *__restrict__ ids) {
+  pdl_trigger();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t token = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   if (token >= num_tokens) return;
@@ -41,7 +43,7 @@ int launch_route(const void *logits, int64_t num_tokens, int num_experts, int to
   const int vpt = (num_experts + 31) / 32;
 #define B200_ROUTE_CASE(V)                                                                  \
   if (vpt <= V) {                                                                           \
-    route_topk_kernel<T, V><<<blocks, threads, 0, stream>>>(lg, num_tokens, num_experts,    \
+    B200_LAUNCH_PDL(kPdlRoute, route_topk_kernel<T, V>, dim3(blocks), dim3(threads), 0, stream, lg, num_tokens, num_experts,    \
                                                            top_k, renormalize, w, ids);    \
     B200_LAUNCHED();                                                                        \
     return B200MOE_OK;                                                                      \

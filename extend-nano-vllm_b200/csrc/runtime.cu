@@ -2,6 +2,7 @@
 // and per-device attribute caches.
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 
 #include "common.cuh"
 
@@ -37,6 +38,15 @@ int sm_count() {
     g_sm_count[dev] = n;
   }
   return g_sm_count[dev];
+}
+
+bool pdl_enabled(unsigned family) {
+  static const unsigned mask = [] {
+    const char *v = getenv("B200MOE_PDL");
+    if (v == nullptr || *v == '\0') return ~0u;
+    return static_cast<unsigned>(strtoul(v, nullptr, 0));
+  }();
+  return (mask & family) != 0;
 }
 
 }  // namespace b200moe

@@ -73,11 +73,12 @@ __device__ __forceinline__ void gate_up_chunk(const __nv_bfloat16 *w_exp, int in
 // NRMAX (1, 2, 4 or 8) bounds the routes handled per chunk.
 template <int VPL, int NRMAX>
 __global__ void __launch_bounds__(kStreamThreads) gate_up_stream_kernel(
-    const __nv_bfloat16 *__restrict__ x, int64_t x_rows, int hidden, int inter,
-    const __nv_bfloat16 *__restrict__ w13, const int32_t *__restrict__ row_route,
-    const int32_t *__restrict__ token_of_route, int top_k, int64_t num_routes,
-    const int32_t *__restrict__ mtiles, const int32_t *__restrict__ counters,
+    const __nv_bfloat16 *x, int64_t x_rows, int hidden, int inter,
+    const __nv_bfloat16 *__restrict__ w13, const int32_t *row_route, const int32_t *token_of_route,
+    int top_k, int64_t num_routes, const int32_t *mtiles, const int32_t *counters,
     __nv_bfloat16 *__restrict__ act) {
+  pdl_trigger();
+  pdl_wait();
   const int tile = blockIdx.x;
   if (tile >= counters[B200MOE_CNT_MTILES]) return;
   const int e = mtiles[tile * B200MOE_MTILE_WORDS + 0];
@@ -171,11 +172,12 @@ __device__ __forceinline__ void down_chunk(const __nv_bfloat16 *w_exp, int hidde
 // grid = (max m-tiles, ceil(H / 32)); VPL >= ceil(I / 256); NRMAX as above.
 template <int VPL, int NRMAX>
 __global__ void __launch_bounds__(kStreamThreads) down_stream_kernel(
-    const __nv_bfloat16 *__restrict__ act, int hidden, int inter,
-    const __nv_bfloat16 *__restrict__ w2, const int32_t *__restrict__ row_route,
-    const __nv_bfloat16 *__restrict__ route_weights, int64_t num_routes,
-    const int32_t *__restrict__ mtiles, const int32_t *__restrict__ counters,
+    const __nv_bfloat16 *act, int hidden, int inter, const __nv_bfloat16 *__restrict__ w2,
+    const int32_t *row_route, const __nv_bfloat16 *route_weights, int64_t num_routes,
+    const int32_t *mtiles, const int32_t *counters,
     __nv_bfloat16 *__restrict__ y) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int RB = VPL == 1 ? 8 : (VPL <= 3 ? 4 : 2);  // rows in flight per warp
   const int tile = blockIdx.x;
   if (tile >= counters[B200MOE_CNT_MTILES]) return;
@@ -248,7 +250,7 @@ int launch_gate_up_stream(dim3 grid, size_t smem, cudaStream_t s, const __nv_bfl
   if (smem > 48 * 1024)
     B200_CUDA(cudaFuncSetAttribute(gate_up_stream_kernel<VPL, NRMAX>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  gate_up_stream_kernel<VPL, NRMAX><<<grid, kStreamThreads, smem, s>>>(
+  B200_LAUNCH_PDL(kPdlStream, gate_up_stream_kernel<VPL, NRMAX>, dim3(grid), dim3(kStreamThreads), smem, s,
       x, x_rows, hidden, inter, w13, row_route, tor, top_k, R, mtiles, counters, act);
   B200_LAUNCHED();
   return B200MOE_OK;
@@ -262,7 +264,7 @@ int launch_down_stream(dim3 grid, size_t smem, cudaStream_t s, const __nv_bfloat
   if (smem > 48 * 1024)
     B200_CUDA(cudaFuncSetAttribute(down_stream_kernel<VPL, NRMAX>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  down_stream_kernel<VPL, NRMAX><<<grid, kStreamThreads, smem, s>>>(act, hidden, inter, w2, row_route,
+  B200_LAUNCH_PDL(kPdlStream, down_stream_kernel<VPL, NRMAX>, dim3(grid), dim3(kStreamThreads), smem, s, act, hidden, inter, w2, row_route,
                                                              rw, R, mtiles, counters, y);
   B200_LAUNCHED();
   return B200MOE_OK;
@@ -280,6 +282,12 @@ constexpr int kTinyWarps = 8;       // gate/up: 8 warps x 4 features per CTA
 constexpr int kTinyFeat = 4;
 constexpr int kTinyDownRows = 8;    // down: 8 output rows per CTA, one warp per route slot
 
+// Asks the TMA unit to pull [p, p + bytes) into L2; p and bytes are multiples
+// of 16.  Nothing waits on it: it only warms L2 for the loads that follow.
+__device__ __forceinline__ void prefetch_l2_bulk(const void *p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ int local_expert(int e, int num_experts, const int64_t *local_index,
                                             int expert_start, int num_local) {
   if (e < 0 || e >= num_experts) return -1;
@@ -295,10 +303,14 @@ __device__ __forceinline__ int local_expert(int e, int num_experts, const int64_
 // in flight ahead; the dot products and SwiGLU are those of gate_up_chunk.
 template <typename TL, int VPT, int VPL>
 __global__ void __launch_bounds__(32 * kTinyWarps) tiny_gate_up_kernel(
-    const TL *__restrict__ logits, const __nv_bfloat16 *__restrict__ x, int hidden, int inter,
-    int num_experts, int top_k, int renormalize, const __nv_bfloat16 *__restrict__ w13,
-    int num_local, const int64_t *__restrict__ local_index, int expert_start,
+    const TL *logits, const __nv_bfloat16 *x, int hidden, int inter, int num_experts,
+    int top_k, int renormalize, const __nv_bfloat16 *__restrict__ w13, int num_local,
+    const int64_t *local_index, int expert_start,
     __nv_bfloat16 *__restrict__ act, int64_t *__restrict__ stats) {
+  // Trigger only once the logits are complete, so the down kernel may read
+  // them before its own wait.
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ uint4 xs[];  // [V]
   __shared__ int s_expert;
   const int route = blockIdx.x;
@@ -363,10 +375,11 @@ __global__ void __launch_bounds__(32 * kTinyWarps) tiny_gate_up_kernel(
 // routes are then summed in fp32 in slot order and stored as bf16.
 template <typename TL, int VPT, int VPL>
 __global__ void __launch_bounds__(512) tiny_down_combine_kernel(
-    const TL *__restrict__ logits, const __nv_bfloat16 *__restrict__ act, int hidden, int inter,
-    int num_experts, int top_k, int renormalize, const __nv_bfloat16 *__restrict__ w2,
-    int num_local, const int64_t *__restrict__ local_index, int expert_start,
+    const TL *logits, const __nv_bfloat16 *act, int hidden, int inter, int num_experts,
+    int top_k, int renormalize, const __nv_bfloat16 *__restrict__ w2, int num_local,
+    const int64_t *local_index, int expert_start,
     __nv_bfloat16 *__restrict__ out) {
+  pdl_trigger();
   constexpr int RB = VPL <= 3 ? 8 : 4;  // rows in flight per warp
   extern __shared__ uint4 as[];  // [top_k][V]
   __shared__ int s_le[16];
@@ -388,13 +401,22 @@ __global__ void __launch_bounds__(512) tiny_down_combine_kernel(
   }
   __syncthreads();
   const int le = s_le[warp];
+  const int h0 = blockIdx.y * kTinyDownRows;
+  // Routing reads only the logits, which were complete before the gate/up
+  // kernel triggered this launch: warm L2 with this CTA's weight rows while
+  // the gate/up kernel still runs, then wait for its activations.
+  if (le >= 0 && lane == 0) {
+    const int nrows = min(kTinyDownRows, hidden - h0);
+    prefetch_l2_bulk(w2 + (static_cast<int64_t>(le) * hidden + h0) * inter,
+                     static_cast<uint32_t>(nrows) * inter * 2);
+  }
+  pdl_wait();
   if (le >= 0) {
     const uint4 *src = reinterpret_cast<const uint4 *>(
         act + (static_cast<int64_t>(token) * top_k + warp) * inter);
     for (int v = lane; v < V; v += 32) as[warp * V + v] = src[v];
   }
   __syncwarp();
-  const int h0 = blockIdx.y * kTinyDownRows;
   if (le >= 0) {
     const __nv_bfloat16 *w_exp = w2 + static_cast<int64_t>(le) * hidden * inter;
 #pragma unroll
@@ -440,7 +462,7 @@ int launch_tiny(const void *logits, const void *x, int64_t num_tokens, int hidde
   if (smem1 > 48 * 1024)
     B200_CUDA(cudaFuncSetAttribute(tiny_gate_up_kernel<TL, VPT, VPLG>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1));
-  tiny_gate_up_kernel<TL, VPT, VPLG><<<g1, 32 * kTinyWarps, smem1, s>>>(
+  B200_LAUNCH_PDL(kPdlTiny, tiny_gate_up_kernel<TL, VPT, VPLG>, dim3(g1), dim3(32 * kTinyWarps), smem1, s,
       lg, static_cast<const __nv_bfloat16 *>(x), hidden, inter, num_experts, top_k, renormalize,
       static_cast<const __nv_bfloat16 *>(w13), num_local, local_index, expert_start,
       static_cast<__nv_bfloat16 *>(act), stats);
@@ -451,7 +473,7 @@ int launch_tiny(const void *logits, const void *x, int64_t num_tokens, int hidde
   if (smem2 > 48 * 1024)
     B200_CUDA(cudaFuncSetAttribute(tiny_down_combine_kernel<TL, VPT, VPLD>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2));
-  tiny_down_combine_kernel<TL, VPT, VPLD><<<g2, 32 * top_k, smem2, s>>>(
+  B200_LAUNCH_PDL(kPdlTiny, tiny_down_combine_kernel<TL, VPT, VPLD>, dim3(g2), dim3(32 * top_k), smem2, s,
       lg, static_cast<const __nv_bfloat16 *>(act), hidden, inter, num_experts, top_k,
       renormalize, static_cast<const __nv_bfloat16 *>(w2), num_local, local_index, expert_start,
       static_cast<__nv_bfloat16 *>(out));

@@ -50,10 +50,16 @@ SMALL = wl.LayerShape("small", 128, 256, 8, 2)
 A = wl.QWEN3_30B_A3B
 
 
-@pytest.mark.parametrize("tokens", [1, 4, 16, 17, 32])
+@pytest.mark.parametrize("tokens,engine", [(1, "auto"), (4, "auto"), (16, "auto"), (17, "auto"),
+                                           (32, "auto"), (16, "stream"), (32, "stream"),
+                                           (16, "tcgen05-wide"), (32, "tcgen05-wide")])
 @torch.inference_mode()
-def test_decode_cuda_graph_replays_changed_inputs(tokens):
+def test_decode_cuda_graph_replays_changed_inputs(tokens, engine):
+    """A replayed graph runs its kernels back to back with programmatic
+    dependent launch, so every kernel's reads of its predecessor's outputs must
+    sit behind its dependency wait; eager runs rarely overlap and miss this."""
     layer, *_ = make_layer(SMALL, 17, graph_safe_decode=True)
+    layer.expert_engine = engine
     hidden = wl.hidden_states(tokens, 128, seed=1).to(DEV)
     first, second = hidden.clone(), wl.hidden_states(tokens, 128, seed=2).to(DEV)
     expected_first, expected_second = layer(first), layer(second)
