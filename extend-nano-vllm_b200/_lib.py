@@ -21,11 +21,13 @@ EUNSUPPORTED = 3
 
 BF16, F16, F32, F64 = 0, 1, 2, 3
 ENGINE_STREAM, ENGINE_TCGEN05, ENGINE_TCGEN05_WIDE, ENGINE_TCGEN05_SWAP = 0, 1, 2, 3
+ENGINE_TCGEN05_PAIR = 4
 MTILE_WORDS = 3
 MTILE_ROWS = 128
+CHUNK_ROWS = 256
 BLOCK_ROWS = 16
-CNT_PADDED_ROWS, CNT_MTILES, CNT_LOCAL_KEPT, CNT_DROPPED = 0, 1, 2, 3
-NUM_COUNTERS = 4
+CNT_PADDED_ROWS, CNT_MTILES, CNT_LOCAL_KEPT, CNT_DROPPED, CNT_CHUNKS = 0, 1, 2, 3, 4
+NUM_COUNTERS = 5
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -42,16 +44,16 @@ SIGNATURES: dict[str, tuple] = {
     "b200moe_pack_row_capacity": (_L, [_L, _I]),
     "b200moe_pack_max_mtiles": (_L, [_L, _I]),
     "b200moe_pack_routes": (_I, [_P, _P, _L, _I, _P, _I, _I, _P, _L, _L, _P, _P, _P, _P, _P,
-                                 _P, _P, _L, _P, _P, _P, _S, _P]),
+                                 _P, _P, _L, _P, _P, _P, _P, _S, _P]),
     "b200moe_pack_static_scratch_capacity": (_S, []),
     "b200moe_pack_routes_static_scratch": (_I, [_P, _P, _L, _I, _P, _I, _I, _P, _L, _L, _P, _P,
                                                 _P, _P, _P, _P, _P, _L, _P, _P, _P]),
     "b200moe_expert_histogram": (_I, [_P, _L, _I, _P, _P]),
     "b200moe_gather_rows": (_I, [_P, _L, _I, _P, _P, _I, _L, _L, _P, _P, _P]),
     "b200moe_expert_gate_up": (_I, [_I, _P, _L, _P, _I, _I, _P, _I, _P, _P, _I, _L, _L, _P,
-                                    _L, _P, _P, _P]),
+                                    _L, _P, _P, _P, _P]),
     "b200moe_expert_down": (_I, [_I, _P, _I, _I, _P, _I, _P, _P, _L, _L, _L, _P, _L, _P, _P,
-                                 _P]),
+                                 _P, _P]),
     "b200moe_decode_tiny": (_I, [_P, _I, _P, _L, _I, _I, _I, _I, _I, _P, _P, _I, _P, _I, _P, _P,
                                  _P, _P]),
     "b200moe_combine": (_I, [_P, _L, _P, _L, _I, _I, _I, _P, _I, _P]),

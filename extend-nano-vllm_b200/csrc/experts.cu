@@ -26,6 +26,13 @@ int tcs_down(const void *act, int hidden, int inter, const void *w2, int num_loc
              const int32_t *row_route, const void *route_weights, int64_t num_routes,
              int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
              const int32_t *counters, void *y, cudaStream_t s);
+int tcp_gate_up(const void *x_packed, int hidden, int inter, const void *w13, int num_local,
+                int64_t row_capacity, const int32_t *chunks, int64_t max_chunks,
+                const int32_t *counters, void *act, cudaStream_t s);
+int tcp_down(const void *act, int hidden, int inter, const void *w2, int num_local,
+             const int32_t *row_route, const void *route_weights, int64_t num_routes,
+             int64_t row_capacity, const int32_t *chunks, int64_t max_chunks,
+             const int32_t *counters, void *y, cudaStream_t s);
 
 namespace {
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -47,8 +54,8 @@ int b200moe_expert_gate_up(int engine, const void *x, int64_t x_rows, const void
                            int hidden, int inter, const void *w13, int num_local_experts,
                            const int32_t *row_route, const int32_t *token_of_route, int top_k,
                            int64_t num_routes, int64_t row_capacity, const int32_t *mtiles,
-                           int64_t max_mtiles, const int32_t *counters, void *act,
-                           void *stream) {
+                           int64_t max_mtiles, const int32_t *chunks, const int32_t *counters,
+                           void *act, void *stream) {
   using namespace b200moe;
   B200_ARG(hidden > 0 && inter > 0 && num_local_experts > 0 && top_k > 0, "bad shape");
   B200_UNSUPPORTED(hidden % 16 == 0 && inter % 16 == 0,
@@ -73,6 +80,12 @@ int b200moe_expert_gate_up(int engine, const void *x, int64_t x_rows, const void
     return tc_gate_up(x_packed, hidden, inter, w13, num_local_experts, num_routes, row_capacity,
                       mtiles, max_mtiles, counters, act, s);
   }
+  if (engine == B200MOE_ENGINE_TCGEN05_PAIR) {
+    B200_ARG(x_packed != nullptr && aligned16(x_packed), "x_packed must be 16-byte aligned");
+    B200_ARG(chunks != nullptr, "the two-SM engine needs the row-chunk list of pack_routes");
+    return tcp_gate_up(x_packed, hidden, inter, w13, num_local_experts, row_capacity, chunks,
+                       max_mtiles, counters, act, s);
+  }
   set_error("unknown engine %d", engine);
   return B200MOE_EINVAL;
 }
@@ -81,8 +94,8 @@ int b200moe_expert_down(int engine, const void *act, int hidden, int inter, cons
                         int num_local_experts, const int32_t *row_route,
                         const void *route_weights, int64_t num_routes, int64_t max_expert_rows,
                         int64_t row_capacity,
-                        const int32_t *mtiles, int64_t max_mtiles, const int32_t *counters,
-                        void *y, void *stream) {
+                        const int32_t *mtiles, int64_t max_mtiles, const int32_t *chunks,
+                        const int32_t *counters, void *y, void *stream) {
   using namespace b200moe;
   B200_ARG(hidden > 0 && inter > 0 && num_local_experts > 0, "bad shape");
   B200_UNSUPPORTED(hidden % 16 == 0 && inter % 16 == 0,
@@ -102,6 +115,11 @@ int b200moe_expert_down(int engine, const void *act, int hidden, int inter, cons
   if (engine == B200MOE_ENGINE_TCGEN05_WIDE)
     return tc_down(act, hidden, inter, w2, num_local_experts, row_route, route_weights,
                    num_routes, row_capacity, mtiles, max_mtiles, counters, y, s);
+  if (engine == B200MOE_ENGINE_TCGEN05_PAIR) {
+    B200_ARG(chunks != nullptr, "the two-SM engine needs the row-chunk list of pack_routes");
+    return tcp_down(act, hidden, inter, w2, num_local_experts, row_route, route_weights,
+                    num_routes, row_capacity, chunks, max_mtiles, counters, y, s);
+  }
   set_error("unknown engine %d", engine);
   return B200MOE_EINVAL;
 }

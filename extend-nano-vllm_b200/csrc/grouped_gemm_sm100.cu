@@ -302,10 +302,14 @@ int make_map(CUtensorMap *map, const void *base, int rank, const uint64_t *dims,
     set_error("cuTensorMapEncodeTiled is unavailable from the CUDA driver");
     return B200MOE_ECUDA;
   }
-  cuuint64_t d[3];
-  cuuint64_t st[2];
-  cuuint32_t bx[3];
-  cuuint32_t es[3] = {1, 1, 1};
+  if (rank < 1 || rank > 5) {
+    set_error("tensor map rank %d out of range", rank);
+    return B200MOE_EINVAL;
+  }
+  cuuint64_t d[5];
+  cuuint64_t st[4];
+  cuuint32_t bx[5];
+  cuuint32_t es[5] = {1, 1, 1, 1, 1};
   for (int i = 0; i < rank; ++i) {
     d[i] = dims[i];
     bx[i] = box[i];

@@ -96,6 +96,7 @@ struct ScatterArgs {
   int32_t *expert_counts;
   int32_t *mtiles;
   int64_t max_mtiles;
+  int32_t *chunks;  // may be null
   int32_t *counters;
   int64_t *stats;
   const int32_t *hist;
@@ -104,7 +105,8 @@ struct ScatterArgs {
 };
 
 // Shared memory (int32 words): base[E1] tot[E1] run[E1] loc[E1]
-// warp_cnt[8][E1] lstart[L] lkept[L] gof[L] mstart[L] + 4 reduction words.
+// warp_cnt[8][E1] lstart[L] lkept[L] gof[L] mstart[L] cstart[L] + 5 reduction
+// words.
 __global__ void __launch_bounds__(kPackThreads) pack_scatter_kernel(ScatterArgs a) {
   pdl_trigger();
   pdl_wait();
@@ -121,7 +123,9 @@ __global__ void __launch_bounds__(kPackThreads) pack_scatter_kernel(ScatterArgs 
   int32_t *lkept = lstart + L;
   int32_t *gof = lkept + L;
   int32_t *mstart = gof + L;
-  int32_t *red = mstart + L;  // [0] kept, [1] dropped, [2] total padded, [3] total mtiles
+  int32_t *cstart = mstart + L;
+  // [0] kept, [1] dropped, [2] total padded, [3] total mtiles, [4] total chunks
+  int32_t *red = cstart + L;
 
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -130,7 +134,7 @@ __global__ void __launch_bounds__(kPackThreads) pack_scatter_kernel(ScatterArgs 
   const int64_t cap = a.capacity < 0 ? (int64_t)0x3fffffffffffffffLL : a.capacity;
 
   for (int i = tid; i < L; i += blockDim.x) gof[i] = -1;
-  if (tid < 4) red[tid] = 0;
+  if (tid < 5) red[tid] = 0;
   for (int i = tid; i < kPackWarps * E1; i += blockDim.x) warp_cnt[i] = 0;
   __syncthreads();
   for (int e = tid; e < E1; e += blockDim.x) {
@@ -159,12 +163,13 @@ __global__ void __launch_bounds__(kPackThreads) pack_scatter_kernel(ScatterArgs 
   __syncthreads();
 
   // Local layout: kept rows per local expert, 16-row padded starts, 128-row
-  // work-tile starts.  Warp 0 scans; each lane owns a contiguous range.
+  // work-tile starts, row-chunk starts.  Warp 0 scans; each lane owns a
+  // contiguous range.
   if (warp == 0) {
     const int per = (L + 31) / 32;
     const int l0 = min(L, lane * per);
     const int l1 = min(L, l0 + per);
-    int64_t rows = 0, tiles = 0;
+    int64_t rows = 0, tiles = 0, chunks = 0;
     for (int l = l0; l < l1; ++l) {
       const int g = gof[l];
       int64_t kept = 0;
@@ -175,28 +180,35 @@ __global__ void __launch_bounds__(kPackThreads) pack_scatter_kernel(ScatterArgs 
       lkept[l] = static_cast<int32_t>(kept);
       rows += (kept + B200MOE_BLOCK_ROWS - 1) / B200MOE_BLOCK_ROWS * B200MOE_BLOCK_ROWS;
       tiles += (kept + B200MOE_MTILE_ROWS - 1) / B200MOE_MTILE_ROWS;
+      chunks += (kept + B200MOE_CHUNK_ROWS - 1) / B200MOE_CHUNK_ROWS;
     }
-    int64_t rows_incl = rows, tiles_incl = tiles;
+    int64_t rows_incl = rows, tiles_incl = tiles, chunks_incl = chunks;
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
       const int64_t r = __shfl_up_sync(0xffffffffu, rows_incl, off);
       const int64_t t = __shfl_up_sync(0xffffffffu, tiles_incl, off);
+      const int64_t c = __shfl_up_sync(0xffffffffu, chunks_incl, off);
       if (lane >= off) {
         rows_incl += r;
         tiles_incl += t;
+        chunks_incl += c;
       }
     }
     int64_t row_off = rows_incl - rows, tile_off = tiles_incl - tiles;
+    int64_t chunk_off = chunks_incl - chunks;
     for (int l = l0; l < l1; ++l) {
       lstart[l] = static_cast<int32_t>(row_off);
       mstart[l] = static_cast<int32_t>(tile_off);
+      cstart[l] = static_cast<int32_t>(chunk_off);
       const int64_t kept = lkept[l];
       row_off += (kept + B200MOE_BLOCK_ROWS - 1) / B200MOE_BLOCK_ROWS * B200MOE_BLOCK_ROWS;
       tile_off += (kept + B200MOE_MTILE_ROWS - 1) / B200MOE_MTILE_ROWS;
+      chunk_off += (kept + B200MOE_CHUNK_ROWS - 1) / B200MOE_CHUNK_ROWS;
     }
     if (lane == 31) {
       red[2] = static_cast<int32_t>(rows_incl);
       red[3] = static_cast<int32_t>(tiles_incl);
+      red[4] = static_cast<int32_t>(chunks_incl);
     }
   }
   __syncthreads();
@@ -204,9 +216,11 @@ __global__ void __launch_bounds__(kPackThreads) pack_scatter_kernel(ScatterArgs 
   if (b == 0) {
     const int32_t total_rows = red[2];
     int32_t total_tiles = red[3];
+    int32_t total_chunks = a.chunks ? red[4] : 0;
     if (total_rows > a.row_capacity || total_tiles > a.max_mtiles) {
       atomicOr(&g_status, kStatusIndex);
       total_tiles = static_cast<int32_t>(min64(total_tiles, a.max_mtiles));
+      total_chunks = static_cast<int32_t>(min64(total_chunks, a.max_mtiles));
     }
     for (int l = tid; l < L; l += blockDim.x) {
       a.expert_offsets[l] = lstart[l];
@@ -224,11 +238,26 @@ __global__ void __launch_bounds__(kPackThreads) pack_scatter_kernel(ScatterArgs 
         a.mtiles[m * B200MOE_MTILE_WORDS + 1] = start + i * B200MOE_MTILE_ROWS;
         a.mtiles[m * B200MOE_MTILE_WORDS + 2] = min(start + (i + 1) * B200MOE_MTILE_ROWS, start + kept);
       }
+      if (a.chunks && kept > 0) {
+        // ceil(kept / 256) chunks of equal 16-row multiples; the last one is
+        // shorter.  Every chunk is non-empty because kept > 256 * (nc - 1).
+        const int32_t nc = (kept + B200MOE_CHUNK_ROWS - 1) / B200MOE_CHUNK_ROWS;
+        const int32_t q = ((kept + nc - 1) / nc + B200MOE_BLOCK_ROWS - 1) / B200MOE_BLOCK_ROWS *
+                          B200MOE_BLOCK_ROWS;
+        for (int32_t i = 0; i < nc; ++i) {
+          const int64_t c = static_cast<int64_t>(cstart[l]) + i;
+          if (c >= a.max_mtiles) break;
+          a.chunks[c * B200MOE_MTILE_WORDS + 0] = l;
+          a.chunks[c * B200MOE_MTILE_WORDS + 1] = start + i * q;
+          a.chunks[c * B200MOE_MTILE_WORDS + 2] = min(start + (i + 1) * q, start + kept);
+        }
+      }
     }
     if (tid == 0) {
       a.expert_offsets[L] = total_rows;
       a.counters[B200MOE_CNT_PADDED_ROWS] = total_rows;
       a.counters[B200MOE_CNT_MTILES] = total_tiles;
+      a.counters[B200MOE_CNT_CHUNKS] = total_chunks;
     }
   }
 
@@ -325,7 +354,7 @@ __global__ void histogram_kernel(const int64_t *__restrict__ ids, int64_t num_ro
 
 size_t scatter_smem_bytes(int num_experts, int num_local) {
   const size_t E1 = static_cast<size_t>(num_experts) + 1;
-  return sizeof(int32_t) * (E1 * (4 + kPackWarps) + 4 * static_cast<size_t>(num_local) + 4);
+  return sizeof(int32_t) * (E1 * (4 + kPackWarps) + 5 * static_cast<size_t>(num_local) + 5);
 }
 
 }  // namespace
@@ -355,8 +384,8 @@ int b200moe_pack_routes(int64_t *expert_ids, void *route_weights, int64_t num_ro
                         int64_t row_capacity, int32_t *row_route, int32_t *route_row,
                         int32_t *combine_rows, int32_t *tile_expert, int32_t *expert_offsets,
                         int32_t *expert_counts, int32_t *mtiles, int64_t max_mtiles,
-                        int32_t *counters, int64_t *stats, void *scratch, size_t scratch_bytes,
-                        void *stream) {
+                        int32_t *chunks, int32_t *counters, int64_t *stats, void *scratch,
+                        size_t scratch_bytes, void *stream) {
   using namespace b200moe;
   B200_ARG(num_routes >= 0 && num_routes < (int64_t)0x7fffffff, "num_routes out of range");
   B200_ARG(num_experts >= 1 && num_experts <= 4096, "num_experts must be in [1, 4096]");
@@ -406,6 +435,7 @@ int b200moe_pack_routes(int64_t *expert_ids, void *route_weights, int64_t num_ro
   a.expert_counts = expert_counts;
   a.mtiles = mtiles;
   a.max_mtiles = max_mtiles;
+  a.chunks = chunks;
   a.counters = counters;
   a.stats = stats;
   a.hist = hist;
@@ -509,8 +539,8 @@ int b200moe_pack_routes_static_scratch(
   return b200moe_pack_routes(expert_ids, route_weights, num_routes, num_experts, local_index,
                              expert_start, num_local_experts, expert_base, capacity,
                              row_capacity, row_route, route_row, combine_rows, tile_expert,
-                             expert_offsets, expert_counts, mtiles, max_mtiles, counters, stats,
-                             scratch, b200moe::kPackStaticScratchBytes, stream);
+                             expert_offsets, expert_counts, mtiles, max_mtiles, nullptr,
+                             counters, stats, scratch, b200moe::kPackStaticScratchBytes, stream);
 }
 
 }  // extern "C"

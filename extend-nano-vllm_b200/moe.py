@@ -219,8 +219,9 @@ class ExpertParallelMoE(nn.Module):
         # Kernel entry points; tests may substitute an object with the same
         # functions to exercise the host logic without a GPU.
         self._ops = _native_ops
-        # "auto" | "stream" | "tcgen05" | "tcgen05-wide" | "tcgen05-swap": expert
-        # GEMM engine ("tcgen05" lets the library pick the variant per call).
+        # "auto" | "stream" | "tcgen05" | "tcgen05-wide" | "tcgen05-swap" |
+        # "tcgen05-pair": expert GEMM engine ("tcgen05" lets the library pick
+        # the variant per call).
         self.expert_engine = "auto"
         # Optional object with begin(name)/end(name) that records CUDA events
         # around the grouped GEMM launches (used by the benchmark).
@@ -445,6 +446,8 @@ class ExpertParallelMoE(nn.Module):
             return _lib.ENGINE_TCGEN05_WIDE
         if self.expert_engine == "tcgen05-swap":
             return _lib.ENGINE_TCGEN05_SWAP
+        if self.expert_engine == "tcgen05-pair":
+            return _lib.ENGINE_TCGEN05_PAIR
         if self.expert_engine != "auto":
             raise ValueError(f"unknown expert engine {self.expert_engine!r}")
         return _lib.ENGINE_STREAM if num_routes <= STREAM_ENGINE_MAX_ROUTES else _lib.ENGINE_TCGEN05

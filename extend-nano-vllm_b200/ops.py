@@ -70,7 +70,8 @@ class PackedRoutes:
     expert_offsets: torch.Tensor  # [E_loc + 1] int32
     expert_counts: torch.Tensor  # [E_loc] int32
     mtiles: torch.Tensor         # [max_mtiles, 3] int32
-    counters: torch.Tensor       # [4] int32
+    counters: torch.Tensor       # [5] int32
+    chunks: torch.Tensor | None = None  # [max_mtiles, 3] int32 row chunks of <= 256 rows
 
 
 def pack_routes(expert_ids: torch.Tensor, route_weights: torch.Tensor | None,
@@ -100,6 +101,7 @@ def pack_routes(expert_ids: torch.Tensor, route_weights: torch.Tensor | None,
     expert_offsets = torch.empty(num_local_experts + 1, **i32)
     expert_counts = torch.empty(num_local_experts, **i32)
     mtiles = torch.empty((max(1, max_mtiles), _lib.MTILE_WORDS), **i32)
+    chunks = torch.empty((max(1, max_mtiles), _lib.MTILE_WORDS), **i32)
     counters = torch.empty(_lib.NUM_COUNTERS, **i32)
     scratch = torch.empty(max(1, scratch_bytes // 4), **i32)
     if local_index is not None:
@@ -114,10 +116,10 @@ def pack_routes(expert_ids: torch.Tensor, route_weights: torch.Tensor | None,
          _p(local_index), int(expert_start), num_local_experts, _p(expert_base),
          -1 if capacity is None else int(capacity), row_capacity, _p(row_route),
          _p(route_row), _p(combine_rows), _p(tile_expert), _p(expert_offsets),
-         _p(expert_counts), _p(mtiles), max_mtiles, _p(counters), _p(stats), _p(scratch),
-         scratch.numel() * 4, _stream(flat))
+         _p(expert_counts), _p(mtiles), max_mtiles, _p(chunks), _p(counters), _p(stats),
+         _p(scratch), scratch.numel() * 4, _stream(flat))
     return PackedRoutes(routes, row_capacity, max_mtiles, row_route, route_row, combine_rows,
-                        tile_expert, expert_offsets, expert_counts, mtiles, counters)
+                        tile_expert, expert_offsets, expert_counts, mtiles, counters, chunks)
 
 
 def expert_histogram(expert_ids: torch.Tensor, num_experts: int) -> torch.Tensor:
@@ -149,7 +151,7 @@ def expert_gate_up(engine: int, x: torch.Tensor, x_packed: torch.Tensor | None,
     call("b200moe_expert_gate_up", engine, _p(x), x.size(0), _p(x_packed), hidden, inter,
          _p(w13), num_local, _p(packed.row_route), _p(token_of_route), top_k,
          packed.num_routes, packed.row_capacity, _p(packed.mtiles), packed.max_mtiles,
-         _p(packed.counters), _p(act), _stream(x))
+         _p(packed.chunks), _p(packed.counters), _p(act), _stream(x))
     return act
 
 
@@ -164,8 +166,8 @@ def expert_down(engine: int, act: torch.Tensor, w2: torch.Tensor, packed: Packed
     y = torch.empty((packed.num_routes, hidden), device=act.device, dtype=torch.bfloat16)
     call("b200moe_expert_down", engine, _p(act), hidden, inter, _p(w2), num_local,
          _p(packed.row_route), _p(route_weights), packed.num_routes, int(max_expert_rows),
-         packed.row_capacity, _p(packed.mtiles), packed.max_mtiles, _p(packed.counters), _p(y),
-         _stream(act))
+         packed.row_capacity, _p(packed.mtiles), packed.max_mtiles, _p(packed.chunks),
+         _p(packed.counters), _p(y), _stream(act))
     return y
 
 

@@ -52,11 +52,17 @@ extern "C" {
                                         128/256-wide weight tiles as N */
 #define B200MOE_ENGINE_TCGEN05_SWAP 3 /* weight rows as the MMA M operand (128 features),
                                         routed rows as N (rounded to 16) */
+#define B200MOE_ENGINE_TCGEN05_PAIR 4 /* two-SM (cta_group::2) swap-AB: 256 weight rows as M,
+                                        row chunks of <= 256 routed rows as N; needs the
+                                        `chunks` list of b200moe_pack_routes */
 
 /* Size of the 128-row work-tile records written by b200moe_pack_routes:
  * {local expert, first packed row, end packed row (exclusive)}. */
 #define B200MOE_MTILE_WORDS 3
 #define B200MOE_MTILE_ROWS 128
+/* Largest row chunk (same record layout): an expert's kept rows split into
+ * ceil(rows / 256) chunks of equal 16-row multiples (the last one shorter). */
+#define B200MOE_CHUNK_ROWS 256
 /* Packing alignment of every expert's row group (reference _MOE_BLOCK_M,
  * nanovllm/layers/moe.py:36). */
 #define B200MOE_BLOCK_ROWS 16
@@ -66,7 +72,8 @@ extern "C" {
 #define B200MOE_CNT_MTILES 1      /* number of 128-row work tiles */
 #define B200MOE_CNT_LOCAL_KEPT 2  /* local assignments, moe.py:864-867 */
 #define B200MOE_CNT_DROPPED 3     /* capacity drops, moe.py:913-917 */
-#define B200MOE_NUM_COUNTERS 4
+#define B200MOE_CNT_CHUNKS 4      /* number of row chunks (0 when `chunks` is NULL) */
+#define B200MOE_NUM_COUNTERS 5
 
 B200MOE_API const char *b200moe_last_error(void);
 B200MOE_API int b200moe_abi_version(void);
@@ -132,7 +139,9 @@ B200MOE_API int64_t b200moe_pack_max_mtiles(int64_t num_routes, int num_local_ex
  *   expert_offsets [E_loc + 1]      first packed row of each local expert; [E_loc] = total
  *   expert_counts  [E_loc]          kept local routes per expert
  *   mtiles         [max_mtiles * 3] 128-row work tiles {expert, row_begin, row_end}
- *   counters       [4]              see B200MOE_CNT_*
+ *   chunks         [max_mtiles * 3] row chunks of <= 256 rows, same records (may be
+ *                                   NULL; the TCGEN05_PAIR engine reads them)
+ *   counters       [5]              see B200MOE_CNT_*
  *   stats          [2] int64 or NULL: += local kept, += dropped (device accumulators)
  */
 B200MOE_API int b200moe_pack_routes(int64_t *expert_ids, void *route_weights, int64_t num_routes,
@@ -141,8 +150,8 @@ B200MOE_API int b200moe_pack_routes(int64_t *expert_ids, void *route_weights, in
                         int64_t capacity, int64_t row_capacity, int32_t *row_route,
                         int32_t *route_row, int32_t *combine_rows, int32_t *tile_expert,
                         int32_t *expert_offsets, int32_t *expert_counts, int32_t *mtiles,
-                        int64_t max_mtiles, int32_t *counters, int64_t *stats,
-                        void *scratch, size_t scratch_bytes, void *stream);
+                        int64_t max_mtiles, int32_t *chunks, int32_t *counters,
+                        int64_t *stats, void *scratch, size_t scratch_bytes, void *stream);
 
 /*
  * b200moe_pack_routes for callers that cannot provide scratch memory.  No
@@ -151,7 +160,8 @@ B200MOE_API int b200moe_pack_routes(int64_t *expert_ids, void *route_weights, in
  * library from plain C / FFI without a device allocator, so the histogram
  * scratch of the packing kernels comes from a static device array inside the
  * library instead of a caller buffer.
- *  - Same arguments and results as b200moe_pack_routes, minus scratch.
+ *  - Same arguments and results as b200moe_pack_routes, minus scratch and
+ *    the row-chunk list (counters[B200MOE_CNT_CHUNKS] = 0).
  *  - Limit: b200moe_pack_static_scratch_capacity() bytes (256 KiB), i.e.
  *    b200moe_pack_scratch_bytes(num_routes, num_experts) must not exceed it;
  *    every call with up to 65,536 routes and up to 1,023 experts fits, and
@@ -206,13 +216,16 @@ B200MOE_API int b200moe_gather_rows(const void *x, int64_t x_rows, int hidden, c
  *   w13   [E_loc, 2I, H] bf16 (gate rows first, moe.py:532-539)
  *   act   [row_capacity, I] bf16 out, packed order
  * engine STREAM reads x ([x_rows, H], token-major) through row_route;
- * engine TCGEN05 reads x_packed ([row_capacity, H], from b200moe_gather_rows).
+ * the TCGEN05 engines read x_packed ([row_capacity, H], from
+ * b200moe_gather_rows).  Work lists: the 128-row `mtiles` (STREAM, WIDE,
+ * SWAP) or the row `chunks` (PAIR; may be NULL for the other engines).
  */
 B200MOE_API int b200moe_expert_gate_up(int engine, const void *x, int64_t x_rows, const void *x_packed,
                            int hidden, int inter, const void *w13, int num_local_experts,
                            const int32_t *row_route, const int32_t *token_of_route, int top_k,
                            int64_t num_routes, int64_t row_capacity, const int32_t *mtiles,
-                           int64_t max_mtiles, const int32_t *counters, void *act, void *stream);
+                           int64_t max_mtiles, const int32_t *chunks, const int32_t *counters,
+                           void *act, void *stream);
 
 /*
  * Grouped down projection with the route-weight scale applied to the fp32
@@ -230,8 +243,8 @@ B200MOE_API int b200moe_expert_down(int engine, const void *act, int hidden, int
                         int num_local_experts, const int32_t *row_route,
                         const void *route_weights, int64_t num_routes, int64_t max_expert_rows,
                         int64_t row_capacity,
-                        const int32_t *mtiles, int64_t max_mtiles, const int32_t *counters,
-                        void *y, void *stream);
+                        const int32_t *mtiles, int64_t max_mtiles, const int32_t *chunks,
+                        const int32_t *counters, void *y, void *stream);
 
 /*
  * Fused expert path for tiny decode batches (num_tokens * top_k <= 16, no

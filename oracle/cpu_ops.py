@@ -43,6 +43,7 @@ class PackedRoutes:
     mtiles: torch.Tensor
     counters: torch.Tensor
     local_ids: np.ndarray
+    chunks: torch.Tensor | None = None
 
 
 class CpuOps:
@@ -70,7 +71,7 @@ class CpuOps:
         lay = mo.pack(flat.numpy(), num_experts, num_local_experts, expert_start, li)
         R = flat.numel()
         counters = torch.tensor([lay["padded_rows"], len(lay["mtiles"]), lay["local_kept"],
-                                 dropped], dtype=torch.int32)
+                                 dropped, len(lay["chunks"])], dtype=torch.int32)
         if stats is not None:
             stats[0] += lay["local_kept"]
             stats[1] += dropped
@@ -81,7 +82,7 @@ class CpuOps:
                             i32(lay["expert_offsets"]), i32(lay["expert_counts"]),
                             i32(lay["mtiles"]), counters,
                             mo.local_ids(flat.numpy(), num_experts, num_local_experts,
-                                         expert_start, li))
+                                         expert_start, li), i32(lay["chunks"]))
 
     def expert_histogram(self, expert_ids, num_experts):
         flat = expert_ids.reshape(-1).numpy()

@@ -29,6 +29,7 @@ import torch
 
 BLOCK_ROWS = 16      # reference _MOE_BLOCK_M, moe.py:36
 MTILE_ROWS = 128     # work-tile rows of the CUDA library
+CHUNK_ROWS = 256     # row-chunk limit of the CUDA library's two-SM engine
 
 
 # ---------------------------------------------------------------------------
@@ -174,7 +175,9 @@ def pack(flat_ids: np.ndarray, num_experts: int, num_local: int, expert_start: i
     padded_rows (num_tokens_post_padded, :807), route_row (dynamic-path
     route_rows with sentinel = row_capacity, :763-767), expert_offsets,
     expert_counts, combine_rows (route id if local else num_routes), mtiles
-    (128-row work tiles of the CUDA library).
+    (128-row work tiles of the CUDA library), chunks (the library's row chunks
+    of <= 256 rows: ceil(n/256) equal 16-row multiples per expert, the last
+    one shorter).
     """
     flat = np.asarray(flat_ids, dtype=np.int64).reshape(-1)
     R = flat.size
@@ -202,10 +205,20 @@ def pack(flat_ids: np.ndarray, num_experts: int, num_local: int, expert_start: i
     for e in range(num_local):
         for i in range(0, int(counts[e]), MTILE_ROWS):
             mtiles.append((e, int(starts[e] + i), int(starts[e] + min(counts[e], i + MTILE_ROWS))))
+    chunks = []
+    for e in range(num_local):
+        n = int(counts[e])
+        if n == 0:
+            continue
+        nc = -(-n // CHUNK_ROWS)
+        q = -(-(-(-n // nc)) // BLOCK_ROWS) * BLOCK_ROWS
+        for i in range(nc):
+            chunks.append((e, int(starts[e] + i * q), int(starts[e] + min(n, (i + 1) * q))))
     return dict(row_route=row_route, tile_expert=tile_expert, padded_rows=total,
                 route_row=route_row, combine_rows=combine_rows,
                 expert_offsets=np.append(starts, total), expert_counts=counts,
                 mtiles=np.array(mtiles, dtype=np.int64).reshape(-1, 3),
+                chunks=np.array(chunks, dtype=np.int64).reshape(-1, 3),
                 local_kept=int(counts.sum()))
 
 

@@ -50,9 +50,9 @@ def test_argument_errors_without_device():
         _lib.call("b200moe_route_topk", null, _lib.F32, 4, 64, 33, 1, null, null, null)
     with pytest.raises(ValueError, match="num_local_experts"):
         _lib.call("b200moe_pack_routes", null, null, 16, 8, null, 0, 9, null, -1, 32, null,
-                  null, null, null, null, null, null, 10, null, null, null, 0, null)
+                  null, null, null, null, null, null, 10, null, null, null, null, 0, null)
     with pytest.raises(NotImplementedError, match="multiples of 16"):
         _lib.call("b200moe_expert_gate_up", 0, null, 1, null, 24, 64, null, 1, null, null, 1, 1,
-                  16, null, 1, null, null, null)
+                  16, null, 1, null, null, null, null)
     with pytest.raises(ValueError, match="ep_size"):
         _lib.call("b200moe_ep_plan", null, 1, 1, 8, null, 17, null, null, null, null)

@@ -105,6 +105,9 @@ def _check_pack(ids_np, num_experts, num_local, expert_start=0, local_index=None
     assert counters[_lib.CNT_LOCAL_KEPT] == lay["local_kept"]
     assert counters[_lib.CNT_DROPPED] == int((~keep).sum())
     np.testing.assert_array_equal(p.mtiles.cpu().numpy()[:n_m], lay["mtiles"])
+    n_c = len(lay["chunks"])
+    assert counters[_lib.CNT_CHUNKS] == n_c
+    np.testing.assert_array_equal(p.chunks.cpu().numpy()[:n_c], lay["chunks"])
     assert stats.tolist() == [lay["local_kept"], int((~keep).sum())]
 
 
@@ -214,7 +217,9 @@ A = wl.QWEN3_30B_A3B
 
 
 ENGINES = [_lib.ENGINE_STREAM, _lib.ENGINE_TCGEN05, _lib.ENGINE_TCGEN05_WIDE,
-           _lib.ENGINE_TCGEN05_SWAP]
+           _lib.ENGINE_TCGEN05_SWAP, _lib.ENGINE_TCGEN05_PAIR]
+TC_ENGINES = [_lib.ENGINE_TCGEN05, _lib.ENGINE_TCGEN05_WIDE, _lib.ENGINE_TCGEN05_SWAP,
+              _lib.ENGINE_TCGEN05_PAIR]
 
 
 @pytest.mark.parametrize("engine", ENGINES)
@@ -224,11 +229,19 @@ def test_expert_engines_match_oracle(engine, shape, tokens):
     _expert_case(shape, tokens, engine, seed=100 + tokens)
 
 
-@pytest.mark.parametrize("engine", [_lib.ENGINE_TCGEN05, _lib.ENGINE_TCGEN05_WIDE,
-                                    _lib.ENGINE_TCGEN05_SWAP])
+@pytest.mark.parametrize("engine", TC_ENGINES)
 def test_tcgen05_prefill_with_capacity_matches_oracle(engine):
     _expert_case(A, 2048, engine, seed=7, logits_kind="zipf",
                  capacity=wl.capacity_for(2048, A, 1.25))
+
+
+@pytest.mark.parametrize("engine", TC_ENGINES)
+@pytest.mark.parametrize("tokens,kind", [(1100, "uniform"), (2048, "zipf")])
+def test_tcgen05_multi_chunk_experts_match_oracle(engine, tokens, kind):
+    """Experts holding more than 256 rows: several row chunks (two-SM engine)
+    or several 128-row tiles; Zipf without capacity piles thousands of rows
+    onto the first experts."""
+    _expert_case(SMALL, tokens, engine, seed=11 + tokens, logits_kind=kind)
 
 
 def test_engines_agree_and_are_repeatable():
