@@ -8,9 +8,9 @@
 // equal 16-row multiples), which becomes the runtime N of the instruction
 // descriptor, so padding stays below 16 rows per chunk.  The two CTAs of a
 // cluster form one M=256 MMA: each loads 128 weight rows (A) and half of the
-// chunk's rows (B) into its own shared memory, so every CTA stages 32 KB per
-// K step for 128 x N x 64 MACs -- a third less shared-memory traffic per MAC
-// than a one-SM 128 x 256 tile.
+// chunk's rows (B) into its own shared memory (the MMA reads the other half
+// from the peer), so each CTA stages at most 32 KB per K step for 128 x N x 64
+// MACs -- a third less L2-to-SM traffic per MAC than a one-SM 128 x 256 tile.
 //
 // Work item = (chunk, weight block).  gate/up: 128 features per pair, each CTA
 // 64, its A tile interleaving 16 gate and 16 up rows per 32-lane TMEM quarter
@@ -21,7 +21,7 @@
 // the leader CTA's full barrier, the leader arms it with the pair's bytes);
 // warp 1 lane 0 of the leader issues tcgen05.mma M=256, N=round16(rows), K=16
 // into one of two TMEM accumulators (256 fp32 columns each, 512 allocated per
-// SM) and commits to both CTAs' barriers; warps 2-5 of each CTA read their
+// SM) and commits to the barriers of both CTAs; warps 2-5 of each CTA read their
 // 128 TMEM lanes, apply SwiGLU (gate/up, reference rounding points moe.py:
 // 742-746, 853-854) or the route-weight scale (down, moe.py:129-139) and store
 // bf16, then arrive on the leader's accumulator-empty barrier.
@@ -30,8 +30,8 @@
 // Every mbarrier wait is bounded; on expiry the CTA records a status bit and
 // its roles leave their loops.  Both CTAs meet at a final cluster barrier
 // before TMEM is freed, so no CTA exits while its peer may still signal it.
-// TMA loads here never multicast; the only multicast is the MMA completion
-// signal (tcgen05.commit) to the pair's barriers.
+// Every TMA load writes only the issuing CTA's shared memory; the MMA
+// completion is signalled to each CTA of the pair by its own commit.
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
@@ -155,14 +155,19 @@ __device__ __forceinline__ void mma_pair(uint32_t d_tmem, uint64_t a_desc, uint6
       : "memory");
 }
 
-// Arrives once on the barrier at offset `bar` of every CTA in `cta_mask` when
-// all MMAs issued so far by this thread have completed.
-__device__ __forceinline__ void commit_pair(uint32_t bar, uint16_t cta_mask) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
-      " [%0], %1;" ::"r"(bar),
-      "h"(cta_mask)
-      : "memory");
+// Arrives once on the mbarrier at cluster address `bar` (this CTA's or the
+// peer's) when all MMAs issued so far by this thread have completed.
+__device__ __forceinline__ void commit_to(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+
+// The same completion signalled to the barrier at local offset `bar` in both
+// CTAs of the pair.
+__device__ __forceinline__ void commit_pair(uint32_t bar) {
+  commit_to(cluster_addr(bar, 0));
+  commit_to(cluster_addr(bar, 1));
 }
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
@@ -306,14 +311,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           for (int kk = 0; kk < BK / 16; ++kk)
             mma_pair(d0, sw128_kmajor_desc(sa + kk * 32), sw128_kmajor_desc(sb + kk * 32), idesc,
                      (kb | kk) != 0 ? 1u : 0u);
-          commit_pair(smem_u32(&empty[stage]), 0x3);
+          commit_pair(smem_u32(&empty[stage]));
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
         if (!ok) break;
-        commit_pair(smem_u32(&acc_full[acc]), 0x3);
+        commit_pair(smem_u32(&acc_full[acc]));
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1;
