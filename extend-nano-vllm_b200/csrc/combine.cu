@@ -68,12 +68,24 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16 *y,
   Acc acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = Acc(0);
-  for (int s = 0; s < top_k; ++s) {
-    const int64_t route = token * top_k + s;
-    const int64_t row = route_rows ? static_cast<int64_t>(route_rows[route]) : route;
-    if (row >= 0 && row < num_rows) {
-      const uint4 v = *reinterpret_cast<const uint4 *>(y + row * hidden + col);
-      const __nv_bfloat162 *vp = reinterpret_cast<const __nv_bfloat162 *>(&v);
+  // Up to 8 slots' rows are loaded before any is summed (independent loads
+  // in flight); the sum itself stays in slot order.
+  for (int s0 = 0; s0 < top_k; s0 += 8) {
+    uint4 v[8];
+    bool ok[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int s = s0 + j;
+      const int64_t route = token * top_k + s;
+      int64_t row = -1;
+      if (s < top_k) row = route_rows ? static_cast<int64_t>(route_rows[route]) : route;
+      ok[j] = row >= 0 && row < num_rows;
+      if (ok[j]) v[j] = *reinterpret_cast<const uint4 *>(y + row * hidden + col);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (!ok[j]) continue;
+      const __nv_bfloat162 *vp = reinterpret_cast<const __nv_bfloat162 *>(&v[j]);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const float2 f = __bfloat1622float2(vp[i]);
@@ -137,7 +149,16 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(
     }
     const uint4 *src = reinterpret_cast<const uint4 *>(x + t * hidden);
     uint4 *dst = reinterpret_cast<uint4 *>(x_packed + p * hidden);
-    for (int v = lane; v < vecs; v += 32) dst[v] = src[v];
+    // Four 16-byte loads in flight per lane before the stores.
+    int v = lane;
+    for (; v + 96 < vecs; v += 128) {
+      const uint4 a = src[v], b = src[v + 32], c = src[v + 64], d = src[v + 96];
+      dst[v] = a;
+      dst[v + 32] = b;
+      dst[v + 64] = c;
+      dst[v + 96] = d;
+    }
+    for (; v < vecs; v += 32) dst[v] = src[v];
   }
 }
 

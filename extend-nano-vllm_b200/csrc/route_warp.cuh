@@ -42,38 +42,45 @@ __device__ __forceinline__ void warp_route_token(const T *row, int num_experts,
 #pragma unroll
   for (int i = 0; i < VPL; ++i) p[i] = p[i] / s;
 
+  // Selection keys: logits mapped to order-preserving unsigned integers
+  // (0 = already taken or not an expert), so each round is one warp max over
+  // the keys and one warp min over the expert ids that hold it.
+  uint32_t key[VPL];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    uint32_t b = __float_as_uint(v[i]);
+    if (b == 0x80000000u) b = 0u;  // -0 ties with +0, as in a float compare
+    key[i] = live[i] ? ((b & 0x80000000u) ? ~b : (b | 0x80000000u)) : 0u;
+  }
   float my_w = 0.f;
   int my_id = 0;
   for (int slot = 0; slot < top_k; ++slot) {
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
-    float bp = 0.f;
+    // This lane's best remaining (largest key, lowest expert id on ties).
+    uint32_t bk = 0u;
+    int bi = 0;
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
-      const int e = lane + 32 * i;
-      if (live[i] && (v[i] > bv || (v[i] == bv && e < bi))) {
-        bv = v[i];
-        bi = e;
-        bp = p[i];
+      if (key[i] > bk) {
+        bk = key[i];
+        bi = i;
       }
     }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-      const float op = __shfl_xor_sync(0xffffffffu, bp, off);
-      if (ov > bv || (ov == bv && oi < bi)) {
-        bv = ov;
-        bi = oi;
-        bp = op;
-      }
-    }
+    const uint32_t kmax = __reduce_max_sync(0xffffffffu, bk);
+    const uint32_t mine = (bk == kmax && kmax != 0u) ? static_cast<uint32_t>(lane + 32 * bi)
+                                                     : 0xffffffffu;
+    const uint32_t win = __reduce_min_sync(0xffffffffu, mine);
+    const int owner = static_cast<int>(win & 31u);
+    float bp = 0.f;
 #pragma unroll
     for (int i = 0; i < VPL; ++i)
-      if (lane + 32 * i == bi) live[i] = false;
+      if (lane == owner && i == static_cast<int>(win >> 5)) {
+        bp = p[i];
+        key[i] = 0u;
+      }
+    bp = __shfl_sync(0xffffffffu, bp, owner);
     if (lane == slot) {
       my_w = bp;
-      my_id = bi;
+      my_id = static_cast<int>(win);
     }
   }
   if (renormalize) {
