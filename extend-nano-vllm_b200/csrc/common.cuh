@@ -241,6 +241,50 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map
       : "memory");
 }
 
+// Where a gate/up GEMM reads its routed rows: a packed copy (x_packed, row p
+// of the packed layout) or, when x_packed is null, the token matrix x through
+// row_route and token_of_route (or route / top_k).
+struct RowSource {
+  const void *x;
+  int64_t x_rows;
+  const void *x_packed;
+  const int32_t *row_route;
+  const int32_t *token_of_route;
+  int top_k;
+  int64_t num_routes;
+};
+
+// Four rows r0..r3 (64 columns from c0) of a 2-D tensor whose map has a
+// one-row box, written as consecutive 128-byte rows at dst (swizzled like a
+// tile load).  Used to read routed rows of the token matrix directly.
+__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap *map, uint32_t bar,
+                                            int c0, int r0, int r1, int r2, int r3) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(r0), "r"(r1), "r"(r2),
+      "r"(r3)
+      : "memory");
+}
+
+// Token row of packed row p for a gathering producer: row_route maps p to a
+// route, the route to its token (token_of_route, else route / top_k).  Rows
+// without a route (padding, past the tile) read token 0; their results are
+// never stored.
+__device__ __forceinline__ int gather_token(int64_t p, int64_t row_end, const int32_t *row_route,
+                                            const int32_t *token_of_route, int top_k,
+                                            int64_t num_routes, int64_t x_rows) {
+  if (p >= row_end) return 0;
+  const int32_t r = row_route[p];
+  if (r < 0 || r >= num_routes) return 0;
+  const int64_t t = token_of_route ? static_cast<int64_t>(token_of_route[r]) : r / top_k;
+  if (t < 0 || t >= x_rows) {
+    atomicOr(&g_status, kStatusIndex);
+    return 0;
+  }
+  return static_cast<int>(t);
+}
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

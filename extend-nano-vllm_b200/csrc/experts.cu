@@ -12,14 +12,14 @@ int stream_down(const void *act, int hidden, int inter, const void *w2, const in
                 const void *route_weights, int64_t num_routes, int64_t max_expert_rows,
                 const int32_t *mtiles, int64_t max_mtiles, const int32_t *counters, void *y,
                 cudaStream_t s);
-int tc_gate_up(const void *x_packed, int hidden, int inter, const void *w13, int num_local,
-               int64_t num_routes, int64_t row_capacity, const int32_t *mtiles,
-               int64_t max_mtiles, const int32_t *counters, void *act, cudaStream_t s);
+int tc_gate_up(const RowSource &src, int hidden, int inter, const void *w13, int num_local,
+               int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
+               const int32_t *counters, void *act, cudaStream_t s);
 int tc_down(const void *act, int hidden, int inter, const void *w2, int num_local,
             const int32_t *row_route, const void *route_weights, int64_t num_routes,
             int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
             const int32_t *counters, void *y, cudaStream_t s);
-int tcs_gate_up(const void *x_packed, int hidden, int inter, const void *w13, int num_local,
+int tcs_gate_up(const RowSource &src, int hidden, int inter, const void *w13, int num_local,
                 int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
                 const int32_t *counters, void *act, cudaStream_t s);
 int tcs_down(const void *act, int hidden, int inter, const void *w2, int num_local,
@@ -70,15 +70,28 @@ int b200moe_expert_gate_up(int engine, const void *x, int64_t x_rows, const void
     return stream_gate_up(x, x_rows, hidden, inter, w13, row_route, token_of_route, top_k,
                           num_routes, mtiles, max_mtiles, counters, act, s);
   }
-  if (engine == B200MOE_ENGINE_TCGEN05_SWAP) {
-    B200_ARG(x_packed != nullptr && aligned16(x_packed), "x_packed must be 16-byte aligned");
-    return tcs_gate_up(x_packed, hidden, inter, w13, num_local_experts, row_capacity, mtiles,
-                       max_mtiles, counters, act, s);
-  }
-  if (engine == B200MOE_ENGINE_TCGEN05_WIDE) {
-    B200_ARG(x_packed != nullptr && aligned16(x_packed), "x_packed must be 16-byte aligned");
-    return tc_gate_up(x_packed, hidden, inter, w13, num_local_experts, num_routes, row_capacity,
-                      mtiles, max_mtiles, counters, act, s);
+  if (engine == B200MOE_ENGINE_TCGEN05_SWAP || engine == B200MOE_ENGINE_TCGEN05_WIDE) {
+    // Rows come from x_packed when given, else straight from x (gathered by
+    // the GEMM's loads through row_route).
+    RowSource src;
+    src.x = x;
+    src.x_rows = x_rows;
+    src.x_packed = x_packed;
+    src.row_route = row_route;
+    src.token_of_route = token_of_route;
+    src.top_k = top_k;
+    src.num_routes = num_routes;
+    if (x_packed != nullptr) {
+      B200_ARG(aligned16(x_packed), "x_packed must be 16-byte aligned");
+    } else {
+      B200_ARG(x != nullptr && aligned16(x) && x_rows > 0,
+               "x must be a 16-byte aligned device pointer with x_rows > 0");
+    }
+    if (engine == B200MOE_ENGINE_TCGEN05_SWAP)
+      return tcs_gate_up(src, hidden, inter, w13, num_local_experts, row_capacity, mtiles,
+                         max_mtiles, counters, act, s);
+    return tc_gate_up(src, hidden, inter, w13, num_local_experts, row_capacity, mtiles,
+                      max_mtiles, counters, act, s);
   }
   if (engine == B200MOE_ENGINE_TCGEN05_PAIR) {
     B200_ARG(x_packed != nullptr && aligned16(x_packed), "x_packed must be 16-byte aligned");

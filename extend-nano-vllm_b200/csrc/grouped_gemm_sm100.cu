@@ -57,6 +57,12 @@ struct Args {
   const int32_t *row_route;
   const __nv_bfloat16 *route_w;
   int64_t num_routes;
+  // gate/up only: gather the A rows from the token matrix (map with a
+  // one-row box) instead of loading 128-row boxes of a packed copy.
+  int gather;
+  const int32_t *token_of_route;
+  int top_k;
+  int64_t x_rows;
 };
 
 __device__ __forceinline__ void store16_bf16(__nv_bfloat16 *dst, const float (&v)[16], int valid) {
@@ -129,24 +135,40 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int num_work = num_mtiles * args.n_tiles;
 
   if (warp == 0) {
-    if (lane == 0) {
-      // ---------------- TMA producer ----------------
-      int stage = 0;
-      uint32_t phase = 0;
-      bool ok = true;
-      for (int w = blockIdx.x; w < num_work && ok; w += gridDim.x) {
-        const int m = w / args.n_tiles;
-        const int n = w - m * args.n_tiles;
-        const int e = args.mtiles[m * B200MOE_MTILE_WORDS + 0];
-        const int rb = args.mtiles[m * B200MOE_MTILE_WORDS + 1];
-        for (int kb = 0; kb < args.num_kb; ++kb) {
-          if (!mbar_wait_bounded(smem_u32(&empty[stage]), phase ^ 1, abort_flag)) {
-            ok = false;
-            break;
-          }
-          const uint32_t fb = smem_u32(&full[stage]);
+    // ---------------- TMA producer (warp 0) ----------------
+    // Lane 0 waits, arms the stage and loads B (and A from a packed copy);
+    // when gathering, lane l loads A rows 4l..4l+3 of the tile.
+    const bool gather = kGateUp && args.gather != 0;
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < num_work && ok; w += gridDim.x) {
+      const int m = w / args.n_tiles;
+      const int n = w - m * args.n_tiles;
+      const int e = args.mtiles[m * B200MOE_MTILE_WORDS + 0];
+      const int rb = args.mtiles[m * B200MOE_MTILE_WORDS + 1];
+      int tok[4] = {0, 0, 0, 0};
+      if (gather) {
+        const int re = args.mtiles[m * B200MOE_MTILE_WORDS + 2];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          tok[j] = gather_token(rb + 4 * lane + j, re, args.row_route, args.token_of_route,
+                                args.top_k, args.num_routes, args.x_rows);
+      }
+      for (int kb = 0; kb < args.num_kb; ++kb) {
+        bool got = true;
+        if (lane == 0) got = mbar_wait_bounded(smem_u32(&empty[stage]), phase ^ 1, abort_flag);
+        if (!__shfl_sync(0xffffffffu, got ? 1 : 0, 0)) {
+          ok = false;
+          break;
+        }
+        const uint32_t fb = smem_u32(&full[stage]);
+        if (gather)
+          tma_gather4(smem_u32(sA + stage * A_BYTES + lane * 4 * BK * 2), &tmA, fb, kb * BK,
+                      tok[0], tok[1], tok[2], tok[3]);
+        if (lane == 0) {
           mbar_arrive_expect_tx(fb, STAGE_BYTES);
-          tma_load_2d(smem_u32(sA + stage * A_BYTES), &tmA, fb, kb * BK, rb);
+          if (!gather) tma_load_2d(smem_u32(sA + stage * A_BYTES), &tmA, fb, kb * BK, rb);
           if (kGateUp) {
             tma_load_3d(smem_u32(sB + stage * B_BYTES), &tmB, fb, kb * BK, n * (BN / 2), 2 * e);
             tma_load_3d(smem_u32(sB + stage * B_BYTES + B_BYTES / 2), &tmB, fb, kb * BK,
@@ -154,10 +176,10 @@ __global__ void __launch_bounds__(THREADS, 1)
           } else {
             tma_load_3d(smem_u32(sB + stage * B_BYTES), &tmB, fb, kb * BK, n * BN, e);
           }
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1;
-          }
+        }
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
         }
       }
     }
@@ -363,15 +385,18 @@ int pick_bn(int64_t num_routes) {
 }
 
 template <int BN>
-int tc_gate_up_bn(const void *x_packed, int hidden, int inter, const void *w13, int num_local,
+int tc_gate_up_bn(const RowSource &src, int hidden, int inter, const void *w13, int num_local,
                   int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
                   const int32_t *counters, void *act, cudaStream_t s) {
   using namespace tcg;
   CUtensorMap ma, mb;
-  const uint64_t da[2] = {static_cast<uint64_t>(hidden), static_cast<uint64_t>(row_capacity)};
+  const bool gather = src.x_packed == nullptr;
+  // Packed copy: 128-row boxes.  Token matrix: one-row boxes for gather4.
+  const uint64_t da[2] = {static_cast<uint64_t>(hidden),
+                          static_cast<uint64_t>(gather ? src.x_rows : row_capacity)};
   const uint64_t sa[1] = {static_cast<uint64_t>(hidden) * 2};
-  const uint32_t ba[2] = {BK, BM};
-  int rc = make_map(&ma, x_packed, 2, da, sa, ba);
+  const uint32_t ba[2] = {BK, gather ? 1u : static_cast<uint32_t>(BM)};
+  int rc = make_map(&ma, gather ? src.x : src.x_packed, 2, da, sa, ba);
   if (rc) return rc;
   // W13 [E, 2I, H] viewed as [2E][I][H]: gate rows of expert e are slab 2e, up rows 2e+1.
   const uint64_t db[3] = {static_cast<uint64_t>(hidden), static_cast<uint64_t>(inter),
@@ -389,9 +414,13 @@ int tc_gate_up_bn(const void *x_packed, int hidden, int inter, const void *w13, 
   a.num_kb = (hidden + BK - 1) / BK;
   a.n_out = inter;
   a.out = static_cast<__nv_bfloat16 *>(act);
-  a.row_route = nullptr;
+  a.row_route = src.row_route;
   a.route_w = nullptr;
-  a.num_routes = 0;
+  a.num_routes = src.num_routes;
+  a.gather = gather ? 1 : 0;
+  a.token_of_route = src.token_of_route;
+  a.top_k = src.top_k;
+  a.x_rows = src.x_rows;
   return launch<true, BN>(ma, mb, a, s);
 }
 
@@ -425,21 +454,25 @@ int tc_down_bn(const void *act, int hidden, int inter, const void *w2, int num_l
   a.row_route = row_route;
   a.route_w = static_cast<const __nv_bfloat16 *>(route_weights);
   a.num_routes = num_routes;
+  a.gather = 0;
+  a.token_of_route = nullptr;
+  a.top_k = 1;
+  a.x_rows = 0;
   return launch<false, BN>(ma, mb, a, s);
 }
 
-int tc_gate_up(const void *x_packed, int hidden, int inter, const void *w13, int num_local,
-               int64_t num_routes, int64_t row_capacity, const int32_t *mtiles,
-               int64_t max_mtiles, const int32_t *counters, void *act, cudaStream_t s) {
-  switch (pick_bn(num_routes)) {
+int tc_gate_up(const RowSource &src, int hidden, int inter, const void *w13, int num_local,
+               int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
+               const int32_t *counters, void *act, cudaStream_t s) {
+  switch (pick_bn(src.num_routes)) {
     case 256:
-      return tc_gate_up_bn<256>(x_packed, hidden, inter, w13, num_local, row_capacity, mtiles,
+      return tc_gate_up_bn<256>(src, hidden, inter, w13, num_local, row_capacity, mtiles,
                                 max_mtiles, counters, act, s);
     case 128:
-      return tc_gate_up_bn<128>(x_packed, hidden, inter, w13, num_local, row_capacity, mtiles,
+      return tc_gate_up_bn<128>(src, hidden, inter, w13, num_local, row_capacity, mtiles,
                                 max_mtiles, counters, act, s);
     default:
-      return tc_gate_up_bn<64>(x_packed, hidden, inter, w13, num_local, row_capacity, mtiles,
+      return tc_gate_up_bn<64>(src, hidden, inter, w13, num_local, row_capacity, mtiles,
                                max_mtiles, counters, act, s);
   }
 }

@@ -62,6 +62,12 @@ struct Args {
   const int32_t *row_route;
   const __nv_bfloat16 *route_w;
   int64_t num_routes;
+  // gate/up only: gather the routed rows from the token matrix (map with a
+  // one-row box) instead of 16-row boxes of a packed copy.
+  int gather;
+  const int32_t *token_of_route;
+  int top_k;
+  int64_t x_rows;
 };
 
 __device__ __forceinline__ void epi_bar() {
@@ -124,26 +130,43 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int num_work = num_mtiles * args.n_blocks;
 
   if (warp == 0) {
-    if (lane == 0) {
-      // ---------------- TMA producer ----------------
-      int stage = 0;
-      uint32_t phase = 0;
-      bool ok = true;
-      for (int w = blockIdx.x; w < num_work && ok; w += gridDim.x) {
-        const int m = w / args.n_blocks;
-        const int fb = w - m * args.n_blocks;
-        const int e = args.mtiles[m * B200MOE_MTILE_WORDS + 0];
-        const int rb = args.mtiles[m * B200MOE_MTILE_WORDS + 1];
-        const int re = args.mtiles[m * B200MOE_MTILE_WORDS + 2];
-        const int nbox = (re - rb + BOX_ROWS - 1) / BOX_ROWS;
-        const uint32_t bytes = C::NW * W_BYTES + nbox * BOX_BYTES;
-        for (int kb = 0; kb < args.num_kb; ++kb) {
-          if (!mbar_wait_bounded(smem_u32(&empty[stage]), phase ^ 1, abort_flag)) {
-            ok = false;
-            break;
-          }
-          uint8_t *st = smem + stage * C::STAGE_BYTES;
-          const uint32_t fbar = smem_u32(&full[stage]);
+    // ---------------- TMA producer (warp 0) ----------------
+    // Lane 0 waits, arms the stage and loads the weight tile(s) (and the rows
+    // of a packed copy); when gathering, lane l loads routed rows 4l..4l+3.
+    const bool gather = kGateUp && args.gather != 0;
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < num_work && ok; w += gridDim.x) {
+      const int m = w / args.n_blocks;
+      const int fb = w - m * args.n_blocks;
+      const int e = args.mtiles[m * B200MOE_MTILE_WORDS + 0];
+      const int rb = args.mtiles[m * B200MOE_MTILE_WORDS + 1];
+      const int re = args.mtiles[m * B200MOE_MTILE_WORDS + 2];
+      const int nbox = (re - rb + BOX_ROWS - 1) / BOX_ROWS;
+      const uint32_t bytes = C::NW * W_BYTES + nbox * BOX_BYTES;
+      const bool my_rows = gather && lane < nbox * (BOX_ROWS / 4);
+      int tok[4] = {0, 0, 0, 0};
+      if (my_rows) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          tok[j] = gather_token(rb + 4 * lane + j, re, args.row_route, args.token_of_route,
+                                args.top_k, args.num_routes, args.x_rows);
+      }
+      for (int kb = 0; kb < args.num_kb; ++kb) {
+        bool got = true;
+        if (lane == 0) got = mbar_wait_bounded(smem_u32(&empty[stage]), phase ^ 1, abort_flag);
+        if (!__shfl_sync(0xffffffffu, got ? 1 : 0, 0)) {
+          ok = false;
+          break;
+        }
+        uint8_t *st = smem + stage * C::STAGE_BYTES;
+        const uint32_t fbar = smem_u32(&full[stage]);
+        uint8_t *sx = st + C::NW * W_BYTES;
+        if (my_rows)
+          tma_gather4(smem_u32(sx + lane * 4 * BK * 2), &tmX, fbar, kb * BK, tok[0], tok[1],
+                      tok[2], tok[3]);
+        if (lane == 0) {
           mbar_arrive_expect_tx(fbar, bytes);
           if (kGateUp) {
             tma_load_3d(smem_u32(st), &tmW, fbar, kb * BK, fb * FM, 2 * e);
@@ -151,13 +174,13 @@ __global__ void __launch_bounds__(THREADS, 1)
           } else {
             tma_load_3d(smem_u32(st), &tmW, fbar, kb * BK, fb * FM, e);
           }
-          uint8_t *sx = st + C::NW * W_BYTES;
-          for (int b = 0; b < nbox; ++b)
-            tma_load_2d(smem_u32(sx + b * BOX_BYTES), &tmX, fbar, kb * BK, rb + b * BOX_ROWS);
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1;
-          }
+          if (!gather)
+            for (int b = 0; b < nbox; ++b)
+              tma_load_2d(smem_u32(sx + b * BOX_BYTES), &tmX, fbar, kb * BK, rb + b * BOX_ROWS);
+        }
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
         }
       }
     }
@@ -310,7 +333,7 @@ int launch(const CUtensorMap &mw, const CUtensorMap &mx, const Args &args, cudaS
 
 }  // namespace tcs
 
-int tcs_gate_up(const void *x_packed, int hidden, int inter, const void *w13, int num_local,
+int tcs_gate_up(const RowSource &src, int hidden, int inter, const void *w13, int num_local,
                 int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
                 const int32_t *counters, void *act, cudaStream_t s) {
   using namespace tcs;
@@ -323,10 +346,13 @@ int tcs_gate_up(const void *x_packed, int hidden, int inter, const void *w13, in
   const uint32_t bw[3] = {BK, FM, 1};
   int rc = tcg::make_map(&mw, w13, 3, dw, sw, bw);
   if (rc) return rc;
-  const uint64_t dx[2] = {static_cast<uint64_t>(hidden), static_cast<uint64_t>(row_capacity)};
+  // Packed copy: 16-row boxes.  Token matrix: one-row boxes for gather4.
+  const bool gather = src.x_packed == nullptr;
+  const uint64_t dx[2] = {static_cast<uint64_t>(hidden),
+                          static_cast<uint64_t>(gather ? src.x_rows : row_capacity)};
   const uint64_t sx[1] = {static_cast<uint64_t>(hidden) * 2};
-  const uint32_t bx[2] = {BK, BOX_ROWS};
-  rc = tcg::make_map(&mx, x_packed, 2, dx, sx, bx);
+  const uint32_t bx[2] = {BK, gather ? 1u : static_cast<uint32_t>(BOX_ROWS)};
+  rc = tcg::make_map(&mx, gather ? src.x : src.x_packed, 2, dx, sx, bx);
   if (rc) return rc;
   Args a;
   a.mtiles = mtiles;
@@ -336,9 +362,13 @@ int tcs_gate_up(const void *x_packed, int hidden, int inter, const void *w13, in
   a.num_kb = (hidden + BK - 1) / BK;
   a.n_out = inter;
   a.out = static_cast<__nv_bfloat16 *>(act);
-  a.row_route = nullptr;
+  a.row_route = src.row_route;
   a.route_w = nullptr;
-  a.num_routes = 0;
+  a.num_routes = src.num_routes;
+  a.gather = gather ? 1 : 0;
+  a.token_of_route = src.token_of_route;
+  a.top_k = src.top_k;
+  a.x_rows = src.x_rows;
   return launch<true>(mw, mx, a, s);
 }
 
@@ -371,6 +401,10 @@ int tcs_down(const void *act, int hidden, int inter, const void *w2, int num_loc
   a.row_route = row_route;
   a.route_w = static_cast<const __nv_bfloat16 *>(route_weights);
   a.num_routes = num_routes;
+  a.gather = 0;
+  a.token_of_route = nullptr;
+  a.top_k = 1;
+  a.x_rows = 0;
   return launch<false>(mw, mx, a, s);
 }
 

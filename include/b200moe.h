@@ -215,10 +215,13 @@ B200MOE_API int b200moe_gather_rows(const void *x, int64_t x_rows, int hidden, c
  *   (moe.py:848-854 and :742-746, kernel moe.py:63-139).
  *   w13   [E_loc, 2I, H] bf16 (gate rows first, moe.py:532-539)
  *   act   [row_capacity, I] bf16 out, packed order
- * engine STREAM reads x ([x_rows, H], token-major) through row_route;
- * the TCGEN05 engines read x_packed ([row_capacity, H], from
- * b200moe_gather_rows).  Work lists: the 128-row `mtiles` (STREAM, WIDE,
- * SWAP) or the row `chunks` (PAIR; may be NULL for the other engines).
+ * engine STREAM reads x ([x_rows, H], token-major) through row_route; the
+ * TCGEN05 engines read x_packed ([row_capacity, H], from b200moe_gather_rows)
+ * when it is not NULL, else (WIDE, SWAP and the per-call choice TCGEN05) the
+ * rows of x directly: the GEMM's TMA loads gather token rows through
+ * row_route and token_of_route (tile::gather4), so no packed copy is
+ * written.  PAIR requires x_packed.  Work lists: the 128-row `mtiles`
+ * (STREAM, WIDE, SWAP) or the row `chunks` (PAIR; may be NULL otherwise).
  */
 B200MOE_API int b200moe_expert_gate_up(int engine, const void *x, int64_t x_rows, const void *x_packed,
                            int hidden, int inter, const void *w13, int num_local_experts,

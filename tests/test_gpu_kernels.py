@@ -183,7 +183,8 @@ def _weights(shape, seed):
     return wl.expert_weights(shape, seed=seed)
 
 
-def _expert_case(shape, tokens, engine, seed, logits_kind="uniform", capacity=None):
+def _expert_case(shape, tokens, engine, seed, logits_kind="uniform", capacity=None,
+                 packed_rows=False):
     w13, w2 = _weights(shape, 11)
     x = wl.hidden_states(tokens, shape.hidden, seed=seed + 1)
     if logits_kind == "uniform":
@@ -198,9 +199,12 @@ def _expert_case(shape, tokens, engine, seed, logits_kind="uniform", capacity=No
                         capacity=capacity)
     if engine == _lib.ENGINE_STREAM:
         act = ops.expert_gate_up(engine, xd, None, w13d, p, shape.top_k)
-    else:
+    elif packed_rows or engine == _lib.ENGINE_TCGEN05_PAIR:
         xp = ops.gather_rows(xd, p, shape.top_k)
         act = ops.expert_gate_up(engine, xd, xp, w13d, p, shape.top_k)
+    else:
+        # One-SM tcgen05 engines gather token rows inside their TMA loads.
+        act = ops.expert_gate_up(engine, xd, None, w13d, p, shape.top_k)
     y = ops.expert_down(engine, act, w2d, p, w.view(-1), tokens)
     out = ops.combine(y, p.combine_rows, tokens, shape.top_k)
     torch.cuda.synchronize()
@@ -242,6 +246,16 @@ def test_tcgen05_multi_chunk_experts_match_oracle(engine, tokens, kind):
     or several 128-row tiles; Zipf without capacity piles thousands of rows
     onto the first experts."""
     _expert_case(SMALL, tokens, engine, seed=11 + tokens, logits_kind=kind)
+
+
+@pytest.mark.parametrize("engine", [_lib.ENGINE_TCGEN05_WIDE, _lib.ENGINE_TCGEN05_SWAP])
+@pytest.mark.parametrize("shape,tokens", [(SMALL, 300), (TINY, 16), (A, 8), (A, 640)])
+def test_fused_row_gather_equals_packed_copy(engine, shape, tokens):
+    """Token rows gathered by the GEMM's TMA loads (tile::gather4) give the
+    same bits as the gate/up GEMM over a packed copy of the rows."""
+    fused = _expert_case(shape, tokens, engine, seed=200 + tokens)
+    packed = _expert_case(shape, tokens, engine, seed=200 + tokens, packed_rows=True)
+    assert torch.equal(fused, packed)
 
 
 def test_engines_agree_and_are_repeatable():
