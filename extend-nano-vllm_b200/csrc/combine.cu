@@ -68,24 +68,12 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16 *y,
   Acc acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = Acc(0);
-  // Up to 8 slots' rows are loaded before any is summed (independent loads
-  // in flight); the sum itself stays in slot order.
-  for (int s0 = 0; s0 < top_k; s0 += 8) {
-    uint4 v[8];
-    bool ok[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int s = s0 + j;
-      const int64_t route = token * top_k + s;
-      int64_t row = -1;
-      if (s < top_k) row = route_rows ? static_cast<int64_t>(route_rows[route]) : route;
-      ok[j] = row >= 0 && row < num_rows;
-      if (ok[j]) v[j] = *reinterpret_cast<const uint4 *>(y + row * hidden + col);
-    }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      if (!ok[j]) continue;
-      const __nv_bfloat162 *vp = reinterpret_cast<const __nv_bfloat162 *>(&v[j]);
+  for (int s = 0; s < top_k; ++s) {
+    const int64_t route = token * top_k + s;
+    const int64_t row = route_rows ? static_cast<int64_t>(route_rows[route]) : route;
+    if (row >= 0 && row < num_rows) {
+      const uint4 v = *reinterpret_cast<const uint4 *>(y + row * hidden + col);
+      const __nv_bfloat162 *vp = reinterpret_cast<const __nv_bfloat162 *>(&v);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const float2 f = __bfloat1622float2(vp[i]);
