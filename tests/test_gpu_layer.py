@@ -273,6 +273,21 @@ def test_tiny_decode_path_matches_unfused_streaming_path(tokens, placement):
     assert layer.dispatch_assignment_count <= 4 * routes
 
 
+@pytest.mark.parametrize("top_k,tokens", [(1, 16), (2, 8), (4, 4), (8, 2), (16, 1)])
+@torch.inference_mode()
+def test_tiny_decode_path_every_token_and_slot(top_k, tokens):
+    """More tokens than warps in a CTA (top_k 1 and 2) and up to 16 slots."""
+    shape = wl.LayerShape("tiny-k", 256, 512, 32, top_k)
+    layer, *_ = make_layer(shape, 80 + top_k)
+    x = wl.hidden_states(tokens, shape.hidden, seed=81).to(DEV)
+    logits = wl.uniform_logits(tokens, shape.num_experts, seed=82).to(DEV)
+    calls = _lib.CALL_COUNTS.get("b200moe_decode_tiny", 0)
+    fused = layer._forward_from_logits(x, logits)
+    assert _lib.CALL_COUNTS.get("b200moe_decode_tiny", 0) == calls + 1
+    layer.expert_engine = "stream"
+    assert torch.equal(fused, layer._forward_from_logits(x, logits))
+
+
 @torch.inference_mode()
 def test_tiny_decode_path_graph_replay():
     layer, *_ = make_layer(SMALL, 71, graph_safe_decode=True)
