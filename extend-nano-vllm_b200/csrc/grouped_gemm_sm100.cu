@@ -74,8 +74,32 @@ __device__ __forceinline__ void store16_bf16(__nv_bfloat16 *dst, const float (&v
     reinterpret_cast<uint4 *>(dst)[0] = o[0];
     reinterpret_cast<uint4 *>(dst)[1] = o[1];
   } else {
-    for (int i = 0; i < valid; ++i) dst[i] = __float2bfloat16_rn(v[i]);
+    // Fully unrolled with a predicate: a loop bounded by `valid` would index
+    // v dynamically and move the array to local memory.
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      if (i < valid) dst[i] = __float2bfloat16_rn(v[i]);
   }
+}
+
+// Waits for this thread's TMEM loads.  The 16 destination registers are tied
+// to the wait so that no use of them can be scheduled before it; tie16 does
+// the same for a second array after the same wait.
+__device__ __forceinline__ void tmem_wait_into(float (&v)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+f"(v[0]), "+f"(v[1]), "+f"(v[2]), "+f"(v[3]), "+f"(v[4]), "+f"(v[5]),
+                 "+f"(v[6]), "+f"(v[7]), "+f"(v[8]), "+f"(v[9]), "+f"(v[10]), "+f"(v[11]),
+                 "+f"(v[12]), "+f"(v[13]), "+f"(v[14]), "+f"(v[15])
+               :
+               : "memory");
+}
+__device__ __forceinline__ void tie16(float (&v)[16]) {
+  asm volatile(""
+               : "+f"(v[0]), "+f"(v[1]), "+f"(v[2]), "+f"(v[3]), "+f"(v[4]), "+f"(v[5]),
+                 "+f"(v[6]), "+f"(v[7]), "+f"(v[8]), "+f"(v[9]), "+f"(v[10]), "+f"(v[11]),
+                 "+f"(v[12]), "+f"(v[13]), "+f"(v[14]), "+f"(v[15])
+               :
+               : "memory");
 }
 
 template <bool kGateUp, int BN>
@@ -247,7 +271,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           float g[16], u[16];
           tmem_ld16(taddr + c, g);
           tmem_ld16(taddr + BN / 2 + c, u);
-          tmem_ld_wait();
+          tmem_wait_into(g);
+          tie16(u);
           const int cols = args.n_out - (col0 + c);
           if (valid && cols > 0) {
             float a[16];
@@ -271,18 +296,29 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int col0 = n * BN;
         __nv_bfloat16 *dst_row =
             args.out + static_cast<int64_t>(route < 0 ? 0 : route) * args.n_out;
+#define B200_EMIT_DOWN(V, C)                                                   \
+  do {                                                                         \
+    const int cols = args.n_out - (col0 + (C));                                \
+    if (route >= 0 && cols > 0) {                                              \
+      _Pragma("unroll") for (int i = 0; i < 16; ++i) V[i] *= rw;               \
+      store16_bf16(dst_row + col0 + (C), V, cols);                             \
+    }                                                                          \
+  } while (0)
+        // Two chunks in flight: the next chunk's TMEM load overlaps the
+        // scaling and stores of the current one.
+        float va[16], vb[16];
+        tmem_ld16(taddr, va);
+        tmem_wait_into(va);
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
-          float v[16];
-          tmem_ld16(taddr + c, v);
-          tmem_ld_wait();
-          const int cols = args.n_out - (col0 + c);
-          if (route >= 0 && cols > 0) {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] *= rw;
-            store16_bf16(dst_row + col0 + c, v, cols);
-          }
+        for (int c = 0; c < BN; c += 32) {
+          tmem_ld16(taddr + c + 16, vb);
+          B200_EMIT_DOWN(va, c);
+          tmem_wait_into(vb);
+          if (c + 32 < BN) tmem_ld16(taddr + c + 32, va);
+          B200_EMIT_DOWN(vb, c + 16);
+          if (c + 32 < BN) tmem_wait_into(va);
         }
+#undef B200_EMIT_DOWN
       }
       tc_fence_before();
       __syncwarp();

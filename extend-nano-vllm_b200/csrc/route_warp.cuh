@@ -70,13 +70,16 @@ __device__ __forceinline__ void warp_route_token(const T *row, int num_experts,
                                                      : 0xffffffffu;
     const uint32_t win = __reduce_min_sync(0xffffffffu, mine);
     const int owner = static_cast<int>(win & 31u);
+    // Selects instead of p[win >> 5]: an index computed at run time would
+    // move p and key to local memory.
+    const int wi = static_cast<int>(win >> 5);
     float bp = 0.f;
 #pragma unroll
-    for (int i = 0; i < VPL; ++i)
-      if (lane == owner && i == static_cast<int>(win >> 5)) {
-        bp = p[i];
-        key[i] = 0u;
-      }
+    for (int i = 0; i < VPL; ++i) {
+      const bool hit = lane == owner && i == wi;
+      bp = hit ? p[i] : bp;
+      key[i] = hit ? 0u : key[i];
+    }
     bp = __shfl_sync(0xffffffffu, bp, owner);
     if (lane == slot) {
       my_w = bp;

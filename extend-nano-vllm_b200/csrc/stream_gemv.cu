@@ -366,7 +366,9 @@ __global__ void __launch_bounds__(32 * kTinyWarps) tiny_gate_up_kernel(
   }
   if (lane == 0) {
     __nv_bfloat16 *dst = act + static_cast<int64_t>(route) * inter + j0;
-    for (int f = 0; f < nfeat; ++f) dst[f] = __float2bfloat16_rn(res[f]);
+#pragma unroll
+    for (int f = 0; f < kTinyFeat; ++f)
+      if (f < nfeat) dst[f] = __float2bfloat16_rn(res[f]);
   }
 }
 
@@ -380,7 +382,9 @@ __global__ void __launch_bounds__(512) tiny_down_combine_kernel(
     const int64_t *local_index, int expert_start,
     __nv_bfloat16 *__restrict__ out) {
   pdl_trigger();
-  constexpr int RB = VPL <= 3 ? 8 : 4;  // rows in flight per warp
+  // Rows in flight per warp, sized so the row buffers (RB * VPL 16-byte
+  // registers) stay within the 128 registers a 512-thread block allows.
+  constexpr int RB = VPL <= 2 ? 8 : (VPL <= 4 ? 4 : 2);
   extern __shared__ uint4 as[];  // [top_k][V]
   __shared__ int s_le[16];
   __shared__ float s_w[16];
