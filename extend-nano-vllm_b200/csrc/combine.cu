@@ -52,7 +52,11 @@ __device__ __forceinline__ void store8<double, double>(double *dst, const double
 }
 
 // One thread per 8 columns of one token.  hidden % 8 == 0.
-template <typename Acc, typename Out>
+// kBatch (small batches, latency-bound): the slot rows of eight routes are
+// requested together before any is summed; otherwise one slot at a time
+// (bandwidth-bound batches keep more threads resident).  The sum is in slot
+// order either way.
+template <typename Acc, typename Out, bool kBatch>
 __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16 *y,
                                                       int64_t num_rows,
                                                       const int32_t *route_rows,
@@ -68,22 +72,45 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16 *y,
   Acc acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = Acc(0);
-  for (int s = 0; s < top_k; ++s) {
-    const int64_t route = token * top_k + s;
-    const int64_t row = route_rows ? static_cast<int64_t>(route_rows[route]) : route;
-    if (row >= 0 && row < num_rows) {
-      const uint4 v = *reinterpret_cast<const uint4 *>(y + row * hidden + col);
-      const __nv_bfloat162 *vp = reinterpret_cast<const __nv_bfloat162 *>(&v);
+  auto add = [&](const uint4 &v) {
+    const __nv_bfloat162 *vp = reinterpret_cast<const __nv_bfloat162 *>(&v);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = __bfloat1622float2(vp[i]);
-        acc[2 * i] += Acc(f.x);
-        acc[2 * i + 1] += Acc(f.y);
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(vp[i]);
+      acc[2 * i] += Acc(f.x);
+      acc[2 * i + 1] += Acc(f.y);
+    }
+  };
+  if constexpr (kBatch) {
+    for (int s0 = 0; s0 < top_k; s0 += 8) {
+      int64_t row[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int64_t route = token * top_k + s0 + j;
+        row[j] = s0 + j >= top_k ? -1
+                 : (route_rows ? static_cast<int64_t>(route_rows[route]) : route);
       }
+      uint4 v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (row[j] >= 0 && row[j] < num_rows)
+          v[j] = *reinterpret_cast<const uint4 *>(y + row[j] * hidden + col);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (row[j] >= 0 && row[j] < num_rows) add(v[j]);
+    }
+  } else {
+    for (int s = 0; s < top_k; ++s) {
+      const int64_t route = token * top_k + s;
+      const int64_t row = route_rows ? static_cast<int64_t>(route_rows[route]) : route;
+      if (row >= 0 && row < num_rows) add(*reinterpret_cast<const uint4 *>(y + row * hidden + col));
     }
   }
   store8<Acc, Out>(out + token * hidden + col, acc);
 }
+
+// Token counts up to which the combine requests all slot rows at once.
+constexpr int64_t kCombineBatchTokens = 256;
 
 template <typename Acc>
 int launch_combine(const void *y, int64_t num_rows, const int32_t *route_rows,
@@ -93,23 +120,31 @@ int launch_combine(const void *y, int64_t num_rows, const int32_t *route_rows,
   const int threads = 256;
   const int64_t blocks = (threads_total + threads - 1) / threads;
   const auto *yp = static_cast<const __nv_bfloat16 *>(y);
+  const bool batch = num_tokens <= kCombineBatchTokens;
+#define B200_COMBINE(OUT)                                                                      \
+  if (batch)                                                                                   \
+    B200_LAUNCH_PDL(kPdlCombine, combine_kernel<Acc, OUT, true>, dim3(blocks), dim3(threads),  \
+                    0, s, yp, num_rows, route_rows, num_tokens, top_k, hidden,                 \
+                    static_cast<OUT *>(out));                                                  \
+  else                                                                                         \
+    B200_LAUNCH_PDL(kPdlCombine, combine_kernel<Acc, OUT, false>, dim3(blocks), dim3(threads), \
+                    0, s, yp, num_rows, route_rows, num_tokens, top_k, hidden,                 \
+                    static_cast<OUT *>(out));
   switch (out_dtype) {
     case B200MOE_BF16:
-      B200_LAUNCH_PDL(kPdlCombine, combine_kernel<Acc, __nv_bfloat16>, dim3(blocks), dim3(threads), 0, s,
-          yp, num_rows, route_rows, num_tokens, top_k, hidden, static_cast<__nv_bfloat16 *>(out));
+      B200_COMBINE(__nv_bfloat16)
       break;
     case B200MOE_F32:
-      B200_LAUNCH_PDL(kPdlCombine, combine_kernel<Acc, float>, dim3(blocks), dim3(threads), 0, s, yp, num_rows, route_rows, num_tokens,
-                                                            top_k, hidden, static_cast<float *>(out));
+      B200_COMBINE(float)
       break;
     case B200MOE_F64:
-      B200_LAUNCH_PDL(kPdlCombine, combine_kernel<Acc, double>, dim3(blocks), dim3(threads), 0, s,
-          yp, num_rows, route_rows, num_tokens, top_k, hidden, static_cast<double *>(out));
+      B200_COMBINE(double)
       break;
     default:
       set_error("unsupported combine output dtype %d", out_dtype);
       return B200MOE_EINVAL;
   }
+#undef B200_COMBINE
   B200_LAUNCHED();
   return B200MOE_OK;
 }
