@@ -352,6 +352,7 @@ def time_e2e(layer, x, steps: int, warmup: int, world: int) -> float:
 def decode_sweep(steps: int, warmup: int, pk: dict) -> list[dict]:
     import extend_nano_vllm_b200.workloads as wl
     from extend_nano_vllm_b200 import STREAM_ENGINE_MAX_ROUTES
+    from extend_nano_vllm_b200.ops import TINY_MAX_ROUTES
 
     shape = wl.QWEN3_30B_A3B
     device = torch.device("cuda")
@@ -393,7 +394,8 @@ def decode_sweep(steps: int, warmup: int, pk: dict) -> list[dict]:
                         "active_experts": active, "algorithmic_bytes": bytes_,
                         "achieved_gbs": round(achieved, 1),
                         "hbm_roofline_frac": round(achieved / pk["hbm_gbs"], 4),
-                        "engine": ("stream" if tokens * shape.top_k <= STREAM_ENGINE_MAX_ROUTES
+                        "engine": ("fused-tiny" if tokens * shape.top_k <= TINY_MAX_ROUTES
+                                   else "stream" if tokens * shape.top_k <= STREAM_ENGINE_MAX_ROUTES
                                    else "tcgen05-swap" if tokens * shape.top_k <= 4096
                                    else "tcgen05-wide")})
         del graph
