@@ -31,90 +31,100 @@ __device__ __forceinline__ int dest_of(int64_t id, int num_experts, const int32_
   return (d >= 0 && d < ep_size) ? d : -1;
 }
 
-// Exclusive scan of each column d of sh[kPlanThreads][N] in place; warp d owns
-// column d, each lane a run of kPlanThreads / 32 consecutive rows.
-__device__ void scan_columns(int32_t *sh, int N, int32_t *totals) {
+// Block-wide exclusive scan of v over the kPlanThreads threads; *total gets
+// the block sum.  warp_tot holds 32 words of shared memory.
+__device__ __forceinline__ int32_t block_exclusive_scan(int32_t v, int32_t *warp_tot,
+                                                        int32_t *total) {
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  if (warp >= N) return;
-  constexpr int kPer = kPlanThreads / 32;
-  int32_t sum = 0;
-  for (int i = 0; i < kPer; ++i) sum += sh[(lane * kPer + i) * N + warp];
-  int32_t incl = sum;
+  int32_t incl = v;
 #pragma unroll
   for (int off = 1; off < 32; off <<= 1) {
-    const int32_t v = __shfl_up_sync(0xffffffffu, incl, off);
-    if (lane >= off) incl += v;
+    const int32_t u = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += u;
   }
-  int32_t run = incl - sum;
-  for (int i = 0; i < kPer; ++i) {
-    const int idx = (lane * kPer + i) * N + warp;
-    const int32_t c = sh[idx];
-    sh[idx] = run;
-    run += c;
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int32_t w = warp_tot[lane];
+    int32_t wi = w;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int32_t u = __shfl_up_sync(0xffffffffu, wi, off);
+      if (lane >= off) wi += u;
+    }
+    warp_tot[lane] = wi - w;  // exclusive warp offsets
+    if (lane == 31) warp_tot[32] = wi;
   }
-  if (lane == 31) totals[warp] = incl;
+  __syncthreads();
+  const int32_t r = warp_tot[warp] + incl - v;
+  *total = warp_tot[32];
+  __syncthreads();  // warp_tot is reused by the next scan
+  return r;
 }
 
-// Single CTA: ordered slots per destination for tokens and routes.
+// Single CTA: ordered slots per destination for tokens and routes.  Tokens
+// are taken kPlanThreads at a time (thread = token, coalesced id loads); for
+// each destination d one block scan of (token sends to d, its routes to d)
+// packed in one word gives the token's slot and its first route slot, in
+// token order (routes: token-major, then slot, i.e. route order).
 __global__ void __launch_bounds__(kPlanThreads) ep_plan_kernel(
     const int64_t *__restrict__ ids, int64_t num_tokens, int top_k, int num_experts,
     const int32_t *__restrict__ owner, int ep_size, int32_t *__restrict__ send_token_slot,
     int32_t *__restrict__ route_dest_slot, int32_t *__restrict__ counts) {
-  extern __shared__ int32_t sh[];  // [kPlanThreads][ep_size] scan buffer
+  __shared__ int32_t warp_tot[33];
+  __shared__ int32_t run_tok[kMaxEp];
+  __shared__ int32_t run_rt[kMaxEp];
+  __shared__ int8_t s_dest[kPlanThreads * 32];  // destinations of the batch's routes
   const int tid = threadIdx.x;
   const int N = ep_size;
-  const int64_t T = num_tokens;
-  const int64_t R = num_tokens * top_k;
-  // Pass A: routes.  Thread tid owns routes [r0, r1).
-  {
-    const int64_t per = (R + kPlanThreads - 1) / kPlanThreads;
-    const int64_t r0 = min(R, tid * per), r1 = min(R, r0 + per);
-    int32_t local[kMaxEp];
-    for (int d = 0; d < N; ++d) local[d] = 0;
-    for (int64_t r = r0; r < r1; ++r) {
-      const int d = dest_of(ids[r], num_experts, owner, N);
-      if (d >= 0) ++local[d];
-    }
-    for (int d = 0; d < N; ++d) sh[tid * N + d] = local[d];
-    __syncthreads();
-    scan_columns(sh, N, counts + N);
-    __syncthreads();
-    for (int d = 0; d < N; ++d) local[d] = sh[tid * N + d];
-    for (int64_t r = r0; r < r1; ++r) {
-      const int d = dest_of(ids[r], num_experts, owner, N);
-      route_dest_slot[r] = d >= 0 ? local[d]++ : -1;
-    }
-    __syncthreads();
+  if (tid < kMaxEp) {
+    run_tok[tid] = 0;
+    run_rt[tid] = 0;
   }
-  // Pass B: tokens.
-  {
-    const int64_t per = (T + kPlanThreads - 1) / kPlanThreads;
-    const int64_t t0 = min(T, tid * per), t1 = min(T, t0 + per);
-    int32_t local[kMaxEp];
-    for (int d = 0; d < N; ++d) local[d] = 0;
-    for (int64_t t = t0; t < t1; ++t) {
-      uint64_t mask = 0;
-      for (int s = 0; s < top_k; ++s) {
-        const int d = dest_of(ids[t * top_k + s], num_experts, owner, N);
-        if (d >= 0) mask |= 1ull << d;
-      }
-      for (int d = 0; d < N; ++d) local[d] += (mask >> d) & 1;
-    }
-    for (int d = 0; d < N; ++d) sh[tid * N + d] = local[d];
+  __syncthreads();
+  for (int64_t t0 = 0; t0 < num_tokens; t0 += kPlanThreads) {
+    const int64_t t = t0 + tid;
+    const bool valid = t < num_tokens;
+    // Destinations of this batch's routes, loaded route-parallel (coalesced).
+    const int64_t r0 = t0 * top_k;
+    const int64_t nr = min64(num_tokens - t0, kPlanThreads) * top_k;
+    for (int64_t i = tid; i < nr; i += kPlanThreads)
+      s_dest[i] = static_cast<int8_t>(dest_of(ids[r0 + i], num_experts, owner, N));
     __syncthreads();
-    scan_columns(sh, N, counts);
-    __syncthreads();
-    for (int d = 0; d < N; ++d) local[d] = sh[tid * N + d];
-    for (int64_t t = t0; t < t1; ++t) {
-      uint64_t mask = 0;
-      for (int s = 0; s < top_k; ++s) {
-        const int d = dest_of(ids[t * top_k + s], num_experts, owner, N);
-        if (d >= 0) mask |= 1ull << d;
+    const int8_t *my_dest = s_dest + static_cast<int64_t>(tid) * top_k;
+    for (int d = 0; d < N; ++d) {
+      int32_t c = 0;
+      if (valid)
+        for (int s = 0; s < top_k; ++s) c += my_dest[s] == d ? 1 : 0;
+      // low 16 bits: routes (<= kPlanThreads * top_k), high: tokens.
+      const int32_t packed = c | ((c > 0 ? 1 : 0) << 16);
+      int32_t total;
+      const int32_t before = block_exclusive_scan(packed, warp_tot, &total);
+      const int32_t tok_slot = run_tok[d] + (before >> 16);
+      int32_t rt_slot = run_rt[d] + (before & 0xffff);
+      if (valid) {
+        send_token_slot[t * N + d] = c > 0 ? tok_slot : -1;
+        if (c > 0)
+          for (int s = 0; s < top_k; ++s)
+            if (my_dest[s] == d) route_dest_slot[t * top_k + s] = rt_slot++;
       }
-      for (int d = 0; d < N; ++d)
-        send_token_slot[t * N + d] = ((mask >> d) & 1) ? local[d]++ : -1;
+      __syncthreads();
+      if (tid == 0) {
+        run_tok[d] += total >> 16;
+        run_rt[d] += total & 0xffff;
+      }
+      __syncthreads();
     }
+    // Routes to no rank (dropped or invalid ids).
+    if (valid)
+      for (int s = 0; s < top_k; ++s)
+        if (my_dest[s] < 0) route_dest_slot[t * top_k + s] = -1;
+    __syncthreads();  // s_dest is refilled by the next batch
+  }
+  if (tid < N) {
+    counts[tid] = run_tok[tid];
+    counts[N + tid] = run_rt[tid];
   }
 }
 
@@ -194,7 +204,7 @@ int b200moe_ep_plan(const int64_t *expert_ids, int64_t num_tokens, int top_k, in
                     int32_t *route_dest_slot, int32_t *counts, void *stream) {
   using namespace b200moe;
   B200_ARG(ep_size >= 1 && ep_size <= kMaxEp, "ep_size must be in [1, %d]", kMaxEp);
-  B200_ARG(num_tokens >= 0 && top_k >= 1 && num_experts >= 1, "bad shape");
+  B200_ARG(num_tokens >= 0 && top_k >= 1 && top_k <= 32 && num_experts >= 1, "bad shape");
   B200_ARG(owner && counts, "null pointer argument");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (num_tokens == 0) {
@@ -202,12 +212,8 @@ int b200moe_ep_plan(const int64_t *expert_ids, int64_t num_tokens, int top_k, in
     return B200MOE_OK;
   }
   B200_ARG(expert_ids && send_token_slot && route_dest_slot, "null pointer argument");
-  const size_t smem = sizeof(int32_t) * kPlanThreads * ep_size;
-  if (smem > 48 * 1024)
-    B200_CUDA(cudaFuncSetAttribute(ep_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   static_cast<int>(smem)));
-  ep_plan_kernel<<<1, kPlanThreads, smem, s>>>(expert_ids, num_tokens, top_k, num_experts, owner,
-                                               ep_size, send_token_slot, route_dest_slot, counts);
+  ep_plan_kernel<<<1, kPlanThreads, 0, s>>>(expert_ids, num_tokens, top_k, num_experts, owner,
+                                            ep_size, send_token_slot, route_dest_slot, counts);
   B200_LAUNCHED();
   return B200MOE_OK;
 }

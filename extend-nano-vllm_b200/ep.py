@@ -129,11 +129,12 @@ def _exchange(layer, x: torch.Tensor) -> torch.Tensor:
         rank = layer.ep_rank
         expert_base = table[:rank, :num_experts].sum(dim=0, dtype=torch.int32).contiguous()
     if tokens:
-        # Capacity pass over this rank's routes: rewrites dropped routes in place.
-        packed_src = layer._pack(ids.view(-1), weights.view(-1), capacity=capacity,
-                                 expert_base=expert_base)
-        if stats is not None:
-            stats[1] += packed_src.counters[_lib.CNT_DROPPED].to(torch.int64)
+        if capacity is not None:
+            # Capacity pass over this rank's routes: rewrites dropped routes in place.
+            packed_src = layer._pack(ids.view(-1), weights.view(-1), capacity=capacity,
+                                     expert_base=expert_base)
+            if stats is not None:
+                stats[1] += packed_src.counters[_lib.CNT_DROPPED].to(torch.int64)
         send_token_slot, route_dest_slot, counts = ops.ep_plan(ids, layer._owner_i32, n,
                                                                num_experts)
     else:
@@ -146,11 +147,12 @@ def _exchange(layer, x: torch.Tensor) -> torch.Tensor:
     dist.all_to_all_single(recv_counts.view(n, 2), counts.view(2, n).t().contiguous(),
                            group=group)
     layer.ep_all_to_all_count += 1
-    send_host = counts.tolist()
-    send_tok, send_rt = send_host[:n], send_host[n:]
-    recv_host = recv_counts.view(n, 2).tolist()
-    recv_tok = [row[0] for row in recv_host]
-    recv_rt = [row[1] for row in recv_host]
+    # One device-to-host read for both count vectors.
+    host = torch.cat([counts, recv_counts]).tolist()
+    send_tok, send_rt = host[:n], host[n:2 * n]
+    recv_host = host[2 * n:]
+    recv_tok = recv_host[0::2]
+    recv_rt = recv_host[1::2]
 
     send_x = torch.empty((sum(send_tok), hidden), device=device, dtype=x.dtype)
     send_meta = torch.empty((sum(send_rt), 4), device=device, dtype=torch.int32)
