@@ -31,52 +31,26 @@ __device__ __forceinline__ int dest_of(int64_t id, int num_experts, const int32_
   return (d >= 0 && d < ep_size) ? d : -1;
 }
 
-// Block-wide exclusive scan of v over the kPlanThreads threads; *total gets
-// the block sum.  warp_tot holds 32 words of shared memory.
-__device__ __forceinline__ int32_t block_exclusive_scan(int32_t v, int32_t *warp_tot,
-                                                        int32_t *total) {
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  int32_t incl = v;
-#pragma unroll
-  for (int off = 1; off < 32; off <<= 1) {
-    const int32_t u = __shfl_up_sync(0xffffffffu, incl, off);
-    if (lane >= off) incl += u;
-  }
-  if (lane == 31) warp_tot[warp] = incl;
-  __syncthreads();
-  if (warp == 0) {
-    const int32_t w = warp_tot[lane];
-    int32_t wi = w;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const int32_t u = __shfl_up_sync(0xffffffffu, wi, off);
-      if (lane >= off) wi += u;
-    }
-    warp_tot[lane] = wi - w;  // exclusive warp offsets
-    if (lane == 31) warp_tot[32] = wi;
-  }
-  __syncthreads();
-  const int32_t r = warp_tot[warp] + incl - v;
-  *total = warp_tot[32];
-  __syncthreads();  // warp_tot is reused by the next scan
-  return r;
-}
-
 // Single CTA: ordered slots per destination for tokens and routes.  Tokens
-// are taken kPlanThreads at a time (thread = token, coalesced id loads); for
-// each destination d one block scan of (token sends to d, its routes to d)
-// packed in one word gives the token's slot and its first route slot, in
-// token order (routes: token-major, then slot, i.e. route order).
+// are taken kPlanThreads at a time (thread = token).  The batch's route
+// destinations are staged in shared memory with coalesced loads; each thread
+// counts its routes per destination, and one block-wide exclusive scan of
+// all destinations at once (token sends in the high 16 bits, routes in the
+// low 16) gives the token's slot and its first route slot per destination,
+// in token order (routes: token-major, then slot, i.e. route order).
 __global__ void __launch_bounds__(kPlanThreads) ep_plan_kernel(
     const int64_t *__restrict__ ids, int64_t num_tokens, int top_k, int num_experts,
     const int32_t *__restrict__ owner, int ep_size, int32_t *__restrict__ send_token_slot,
     int32_t *__restrict__ route_dest_slot, int32_t *__restrict__ counts) {
-  __shared__ int32_t warp_tot[33];
+  constexpr int kWarps = kPlanThreads / 32;
+  __shared__ int32_t warp_tot[kWarps][kMaxEp];  // per-warp sums, then warp offsets
+  __shared__ int32_t batch_tot[kMaxEp];
   __shared__ int32_t run_tok[kMaxEp];
   __shared__ int32_t run_rt[kMaxEp];
   __shared__ int8_t s_dest[kPlanThreads * 32];  // destinations of the batch's routes
   const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
   const int N = ep_size;
   if (tid < kMaxEp) {
     run_tok[tid] = 0;
@@ -86,41 +60,75 @@ __global__ void __launch_bounds__(kPlanThreads) ep_plan_kernel(
   for (int64_t t0 = 0; t0 < num_tokens; t0 += kPlanThreads) {
     const int64_t t = t0 + tid;
     const bool valid = t < num_tokens;
-    // Destinations of this batch's routes, loaded route-parallel (coalesced).
     const int64_t r0 = t0 * top_k;
     const int64_t nr = min64(num_tokens - t0, kPlanThreads) * top_k;
     for (int64_t i = tid; i < nr; i += kPlanThreads)
       s_dest[i] = static_cast<int8_t>(dest_of(ids[r0 + i], num_experts, owner, N));
     __syncthreads();
     const int8_t *my_dest = s_dest + static_cast<int64_t>(tid) * top_k;
-    for (int d = 0; d < N; ++d) {
-      int32_t c = 0;
-      if (valid)
-        for (int s = 0; s < top_k; ++s) c += my_dest[s] == d ? 1 : 0;
-      // low 16 bits: routes (<= kPlanThreads * top_k), high: tokens.
-      const int32_t packed = c | ((c > 0 ? 1 : 0) << 16);
-      int32_t total;
-      const int32_t before = block_exclusive_scan(packed, warp_tot, &total);
-      const int32_t tok_slot = run_tok[d] + (before >> 16);
-      int32_t rt_slot = run_rt[d] + (before & 0xffff);
-      if (valid) {
-        send_token_slot[t * N + d] = c > 0 ? tok_slot : -1;
+    // Per destination: routes (low 16 bits, <= kPlanThreads * 32 in a batch)
+    // and the token itself (high bits).
+    int32_t v[kMaxEp];
+#pragma unroll
+    for (int d = 0; d < kMaxEp; ++d) v[d] = 0;
+    if (valid)
+      for (int s = 0; s < top_k; ++s) {
+        const int ds = my_dest[s];
+#pragma unroll
+        for (int d = 0; d < kMaxEp; ++d) v[d] += ds == d ? 1 : 0;
+      }
+#pragma unroll
+    for (int d = 0; d < kMaxEp; ++d) v[d] |= (v[d] > 0 ? 1 : 0) << 16;
+    int32_t incl[kMaxEp];
+#pragma unroll
+    for (int d = 0; d < kMaxEp; ++d) {
+      int32_t x = v[d];
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int32_t u = __shfl_up_sync(0xffffffffu, x, off);
+        if (lane >= off) x += u;
+      }
+      incl[d] = x;
+    }
+    if (lane == 31) {
+#pragma unroll
+      for (int d = 0; d < kMaxEp; ++d) warp_tot[warp][d] = incl[d];
+    }
+    __syncthreads();
+    if (warp < N) {  // warp d scans destination d across the kWarps warps
+      const int32_t w = warp_tot[lane][warp];
+      int32_t wi = w;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int32_t u = __shfl_up_sync(0xffffffffu, wi, off);
+        if (lane >= off) wi += u;
+      }
+      warp_tot[lane][warp] = wi - w;
+      if (lane == 31) batch_tot[warp] = wi;
+    }
+    __syncthreads();
+    if (valid) {
+#pragma unroll
+      for (int d = 0; d < kMaxEp; ++d) {
+        if (d >= N) break;
+        const int32_t before = warp_tot[warp][d] + incl[d] - v[d];
+        const int32_t c = v[d] & 0xffff;
+        send_token_slot[t * N + d] = c > 0 ? run_tok[d] + (before >> 16) : -1;
+        int32_t slot = run_rt[d] + (before & 0xffff);
         if (c > 0)
           for (int s = 0; s < top_k; ++s)
-            if (my_dest[s] == d) route_dest_slot[t * top_k + s] = rt_slot++;
+            if (my_dest[s] == d) route_dest_slot[t * top_k + s] = slot++;
       }
-      __syncthreads();
-      if (tid == 0) {
-        run_tok[d] += total >> 16;
-        run_rt[d] += total & 0xffff;
-      }
-      __syncthreads();
-    }
-    // Routes to no rank (dropped or invalid ids).
-    if (valid)
+      // Routes to no rank (dropped or invalid ids).
       for (int s = 0; s < top_k; ++s)
         if (my_dest[s] < 0) route_dest_slot[t * top_k + s] = -1;
-    __syncthreads();  // s_dest is refilled by the next batch
+    }
+    __syncthreads();
+    if (tid < N) {
+      run_tok[tid] += batch_tot[tid] >> 16;
+      run_rt[tid] += batch_tot[tid] & 0xffff;
+    }
+    __syncthreads();  // s_dest, warp_tot and the running offsets are reused
   }
   if (tid < N) {
     counts[tid] = run_tok[tid];

@@ -258,6 +258,24 @@ def test_fused_row_gather_equals_packed_copy(engine, shape, tokens):
     assert torch.equal(fused, packed)
 
 
+@pytest.mark.parametrize("tokens,top_k,ep_size", [(1, 8, 2), (300, 8, 4), (4096, 8, 8),
+                                                   (2500, 2, 16), (1030, 32, 3)])
+def test_ep_plan_slots_match_cpu_plan(tokens, top_k, ep_size):
+    """Per-destination token and route slots (token order, route order) and
+    the counts, against the CPU restatement; includes invalid ids."""
+    from oracle.cpu_ops import CpuOps
+    num_experts = 64
+    gen = torch.Generator().manual_seed(tokens + ep_size)
+    ids = torch.randint(-1, num_experts + 1, (tokens, top_k), generator=gen)
+    owner = torch.randint(0, ep_size, (num_experts,), generator=gen).to(torch.int32)
+    tok_d, rt_d, cnt_d = ops.ep_plan(ids.to(DEV), owner.to(DEV), ep_size, num_experts)
+    tok_c, rt_c, cnt_c = CpuOps().ep_plan(ids, owner, ep_size, num_experts)
+    torch.cuda.synchronize()
+    assert torch.equal(tok_d.cpu(), tok_c)
+    assert torch.equal(rt_d.cpu(), rt_c)
+    assert torch.equal(cnt_d.cpu(), cnt_c)
+
+
 def test_engines_agree_and_are_repeatable():
     outs = [_expert_case(A, 16, e, seed=3) for e in ENGINES]
     for other in outs[1:]:
