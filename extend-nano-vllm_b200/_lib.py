@@ -59,7 +59,7 @@ SIGNATURES: dict[str, tuple] = {
     "b200moe_combine": (_I, [_P, _L, _P, _L, _I, _I, _I, _P, _I, _P]),
     "b200moe_ep_plan": (_I, [_P, _L, _I, _I, _P, _I, _P, _P, _P, _P]),
     "b200moe_ep_pack": (_I, [_P, _I, _P, _P, _L, _I, _I, _P, _I, _P, _P, _P, _P, _P, _P, _P]),
-    "b200moe_ep_unpack_routes": (_I, [_P, _L, _I, _P, _P, _P, _P, _P, _P]),
+    "b200moe_ep_unpack_routes": (_I, [_P, _L, _I, _P, _P, _P, _P, _P, _P, _P]),
     "b200moe_ep_return_rows": (_I, [_P, _P, _L, _I, _I, _P, _P, _L, _P, _P]),
 }
 

@@ -171,13 +171,14 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(
 
 __global__ void ep_unpack_kernel(const int4 *__restrict__ meta, int64_t n, int ep_size,
                                  Offsets recv_route_off, Offsets recv_tok_off,
-                                 int64_t *__restrict__ ids, int32_t *__restrict__ token_of_route,
+                                 Offsets meta_start, int64_t *__restrict__ ids,
+                                 int32_t *__restrict__ token_of_route,
                                  __nv_bfloat16 *__restrict__ rw) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
   int src = 0;
   while (src + 1 < ep_size && i >= recv_route_off.v[src + 1]) ++src;
-  const int4 m = meta[i];
+  const int4 m = meta[meta_start.v[src] + (i - recv_route_off.v[src])];
   ids[i] = m.x;
   token_of_route[i] = recv_tok_off.v[src] + m.y;
   rw[i] = __ushort_as_bfloat16(static_cast<unsigned short>(m.z & 0xffff));
@@ -256,7 +257,8 @@ int b200moe_ep_pack(const void *x, int hidden, const int64_t *expert_ids,
 
 int b200moe_ep_unpack_routes(const int32_t *recv_meta, int64_t num_recv_routes, int ep_size,
                              const int32_t *recv_route_offsets_host,
-                             const int32_t *recv_token_offsets_host, int64_t *expert_ids,
+                             const int32_t *recv_token_offsets_host,
+                             const int32_t *recv_meta_starts_host, int64_t *expert_ids,
                              int32_t *token_of_route, void *route_weights, void *stream) {
   using namespace b200moe;
   B200_ARG(ep_size >= 1 && ep_size <= kMaxEp, "ep_size must be in [1, %d]", kMaxEp);
@@ -264,13 +266,17 @@ int b200moe_ep_unpack_routes(const int32_t *recv_meta, int64_t num_recv_routes, 
   B200_ARG(recv_meta && recv_route_offsets_host && recv_token_offsets_host && expert_ids &&
                token_of_route && route_weights,
            "null pointer argument");
-  Offsets ro, to;
+  Offsets ro, to, ms;
   load_offsets(ro, recv_route_offsets_host, ep_size + 1);
   load_offsets(to, recv_token_offsets_host, ep_size);
+  // Records of each source are contiguous at recv_meta + start[s] (default:
+  // all sources back to back).
+  load_offsets(ms, recv_meta_starts_host ? recv_meta_starts_host : recv_route_offsets_host,
+               ep_size);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t blocks = (num_recv_routes + 255) / 256;
   ep_unpack_kernel<<<blocks, 256, 0, s>>>(reinterpret_cast<const int4 *>(recv_meta),
-                                          num_recv_routes, ep_size, ro, to, expert_ids,
+                                          num_recv_routes, ep_size, ro, to, ms, expert_ids,
                                           token_of_route,
                                           static_cast<__nv_bfloat16 *>(route_weights));
   B200_LAUNCHED();

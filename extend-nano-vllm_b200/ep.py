@@ -154,24 +154,31 @@ def _exchange(layer, x: torch.Tensor) -> torch.Tensor:
     recv_tok = recv_host[0::2]
     recv_rt = recv_host[1::2]
 
-    send_x = torch.empty((sum(send_tok), hidden), device=device, dtype=x.dtype)
-    send_meta = torch.empty((sum(send_rt), 4), device=device, dtype=torch.int32)
+    # One payload per peer: its token rows, then its 16-byte route records
+    # padded to whole rows, so a single all-to-all carries both.
+    per_row = hidden * x.element_size() // 16  # route records per row
+    send_rows = [send_tok[d] + -(-send_rt[d] // per_row) for d in range(n)]
+    recv_rows = [recv_tok[s] + -(-recv_rt[s] // per_row) for s in range(n)]
+    send_row0, recv_row0 = _prefix(send_rows), _prefix(recv_rows)
+    send_buf = torch.empty((sum(send_rows), hidden), device=device, dtype=x.dtype)
     if tokens:
         ops.ep_pack(x, ids, weights, layer._owner_i32, n, num_experts, send_token_slot,
-                    route_dest_slot, _prefix(send_tok), _prefix(send_rt), send_x, send_meta)
-    recv_x = torch.empty((sum(recv_tok), hidden), device=device, dtype=x.dtype)
-    recv_meta = torch.empty((sum(recv_rt), 4), device=device, dtype=torch.int32)
-    dist.all_to_all_single(recv_x, send_x, recv_tok, send_tok, group=group)
-    dist.all_to_all_single(recv_meta, send_meta, recv_rt, send_rt, group=group)
-    layer.ep_all_to_all_count += 2
+                    route_dest_slot, send_row0,
+                    [(send_row0[d] + send_tok[d]) * per_row for d in range(n)], send_buf,
+                    send_buf.view(torch.int32).view(-1, 4))
+    recv_buf = torch.empty((sum(recv_rows), hidden), device=device, dtype=x.dtype)
+    dist.all_to_all_single(recv_buf, send_buf, recv_rows, send_rows, group=group)
+    layer.ep_all_to_all_count += 1
     layer.total_dispatch_token_count += sum(send_tok)
 
-    num_recv = recv_meta.size(0)
+    num_recv = sum(recv_rt)
     if num_recv:
         r_ids, token_of_route, r_w = ops.ep_unpack_routes(
-            recv_meta, n, _prefix(recv_rt) + [sum(recv_rt)], _prefix(recv_tok))
+            recv_buf.view(torch.int32).view(-1, 4), n, _prefix(recv_rt) + [num_recv],
+            recv_row0, [(recv_row0[s] + recv_tok[s]) * per_row for s in range(n)],
+            num_records=num_recv)
         packed = layer._pack(r_ids, None, stats=stats)
-        y_local = layer._run_experts(recv_x, r_w, packed, 1, token_of_route)
+        y_local = layer._run_experts(recv_buf, r_w, packed, 1, token_of_route)
     else:
         y_local = torch.empty((0, hidden), device=device, dtype=torch.bfloat16)
     returned = torch.empty((sum(send_rt), hidden), device=device, dtype=torch.bfloat16)

@@ -233,15 +233,19 @@ def ep_pack(x, expert_ids, route_weights, owner, ep_size, num_experts, send_toke
          _stream(x))
 
 
-def ep_unpack_routes(recv_meta, ep_size, recv_route_offsets, recv_token_offsets):
-    n = recv_meta.size(0)
+def ep_unpack_routes(recv_meta, ep_size, recv_route_offsets, recv_token_offsets,
+                     recv_meta_starts=None, num_records=None):
+    """recv_meta: [n, 4] int32 records, or (with recv_meta_starts) any buffer
+    holding each source's records at those 16-byte record indices."""
+    n = recv_meta.size(0) if num_records is None else int(num_records)
     device = recv_meta.device
     ids = torch.empty(n, device=device, dtype=torch.int64)
     token_of_route = torch.empty(n, device=device, dtype=torch.int32)
     weights = torch.empty(n, device=device, dtype=torch.bfloat16)
     call("b200moe_ep_unpack_routes", _p(recv_meta), n, ep_size, _host_i32(recv_route_offsets),
-         _host_i32(recv_token_offsets), _p(ids), _p(token_of_route), _p(weights),
-         _stream(recv_meta))
+         _host_i32(recv_token_offsets),
+         None if recv_meta_starts is None else _host_i32(recv_meta_starts), _p(ids),
+         _p(token_of_route), _p(weights), _stream(recv_meta))
     return ids, token_of_route, weights
 
 

@@ -315,12 +315,16 @@ B200MOE_API int b200moe_ep_pack(const void *x, int hidden, const int64_t *expert
  * Receiver: expand received route records into the flat arrays the local
  * pipeline consumes.  recv_route_offsets_host [ep_size + 1] and
  * recv_token_offsets_host [ep_size] are HOST prefix sums of what each source
- * sent.  Outputs: expert_ids (global ids), token_of_route (row in the received
- * token buffer), route_weights (bf16).
+ * sent (records; token rows).  recv_meta_starts_host [ep_size] (HOST, may be
+ * NULL = recv_route_offsets_host) is the 16-byte record index in recv_meta
+ * where each source's records start, so records may sit inside a combined
+ * payload buffer.  Outputs: expert_ids (global ids), token_of_route (row in
+ * the received token buffer), route_weights (bf16).
  */
 B200MOE_API int b200moe_ep_unpack_routes(const int32_t *recv_meta, int64_t num_recv_routes, int ep_size,
                              const int32_t *recv_route_offsets_host,
-                             const int32_t *recv_token_offsets_host, int64_t *expert_ids,
+                             const int32_t *recv_token_offsets_host,
+                             const int32_t *recv_meta_starts_host, int64_t *expert_ids,
                              int32_t *token_of_route, void *route_weights, void *stream);
 
 /*

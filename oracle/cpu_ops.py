@@ -180,11 +180,16 @@ class CpuOps:
                 send_meta[route_offsets[d] + rs[r]] = torch.tensor(
                     [int(ids[r]), int(tok_slot[r // k, d]), int(bits[r]), r], dtype=torch.int32)
 
-    def ep_unpack_routes(self, recv_meta, ep_size, recv_route_offsets, recv_token_offsets):
+    def ep_unpack_routes(self, recv_meta, ep_size, recv_route_offsets, recv_token_offsets,
+                         recv_meta_starts=None, num_records=None):
         meta = recv_meta.numpy()
-        n = meta.shape[0]
+        n = meta.shape[0] if num_records is None else int(num_records)
         src = np.searchsorted(np.asarray(recv_route_offsets[1:ep_size]), np.arange(n),
                               side="right")
+        if recv_meta_starts is not None:
+            pos = (np.asarray(recv_meta_starts)[src]
+                   + np.arange(n) - np.asarray(recv_route_offsets)[src])
+            meta = meta[pos]
         ids = torch.from_numpy(meta[:, 0].astype(np.int64))
         tor = torch.from_numpy((np.asarray(recv_token_offsets)[src] + meta[:, 1]).astype(np.int32))
         w = torch.from_numpy((meta[:, 2] & 0xFFFF).astype(np.int16)).view(torch.bfloat16)
