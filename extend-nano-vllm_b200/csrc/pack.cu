@@ -139,6 +139,9 @@ __global__ void __launch_bounds__(kPackThreads) pack_scatter_kernel(ScatterArgs 
   __syncthreads();
   for (int e = tid; e < E1; e += blockDim.x) {
     int32_t before = 0, all = 0;
+    // Independent loads: unrolled so several are in flight (this prefix over
+    // the blocks' histograms is the scatter kernel's critical path).
+#pragma unroll 8
     for (int bb = 0; bb < a.nblk; ++bb) {
       const int32_t h = a.hist[static_cast<int64_t>(bb) * E1 + e];
       if (bb < b) before += h;
