@@ -18,7 +18,8 @@ synchronize around the timed region, max over ranks.  Expert weights
 
 At N = 1, rank 0 also reports (``sweep``) the decode buckets T in
 {1, 8, 32, 64, 128, 256, 512} of the 30B-A3B layer (uniform fp32 logits, one
-CUDA graph per bucket, L2 flushed before every replay) and the T=8192
+CUDA graph per bucket, L2 flushed before every replay by writing and then
+reading 256 MB buffers) and the T=8192
 chunked-prefill batch with Zipf(1.2) expert popularity and capacity factor
 1.25, each against its roofline; and a CPU baseline: the reference's own
 CPU algorithm (softmax/top-k and the per-expert torch loop of
@@ -357,7 +358,13 @@ def decode_sweep(steps: int, warmup: int, pk: dict) -> list[dict]:
     shape = wl.QWEN3_30B_A3B
     device = torch.device("cuda")
     layer = build_layer(shape, 1, 0, device, graph_safe_decode=True)
+    # L2 flush between replays: write 256 MB (evicts everything), then read
+    # another 256 MB, so that the replay starts with none of the layer's data
+    # in L2 and with clean lines only.  A write-only flush leaves up to L2's
+    # size of dirty lines whose write-back then lands inside the timed replay;
+    # that variant is timed too and reported as "ms_dirty_l2".
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    flush_read = torch.ones(256 * 1024 * 1024, dtype=torch.uint8, device=device)
     results = []
     for tokens in DECODE_BUCKETS:
         x = wl.hidden_states(tokens, shape.hidden, seed=300 + tokens, device=device)
@@ -373,23 +380,28 @@ def decode_sweep(steps: int, warmup: int, pk: dict) -> list[dict]:
             layer._forward_from_logits(x, logits)
         for _ in range(warmup):
             graph.replay()
-        times = []
-        for _ in range(steps):
-            flush.fill_(1)  # evict the previous replay's weights from L2
-            a = torch.cuda.Event(enable_timing=True)
-            b = torch.cuda.Event(enable_timing=True)
-            a.record()
-            graph.replay()
-            b.record()
-            times.append((a, b))
+        times, dirty = [], []
+        for clean in (True, False):
+            for _ in range(steps):
+                flush.fill_(1)  # evict the previous replay's weights from L2
+                if clean:
+                    flush_read.amax()
+                a = torch.cuda.Event(enable_timing=True)
+                b = torch.cuda.Event(enable_timing=True)
+                a.record()
+                graph.replay()
+                b.record()
+                (times if clean else dirty).append((a, b))
         torch.cuda.synchronize()
         ms = statistics.median(a.elapsed_time(b) for a, b in times)
+        ms_dirty = statistics.median(a.elapsed_time(b) for a, b in dirty)
         ids = torch.topk(logits, shape.top_k, dim=-1).indices
         active = int(torch.unique(ids).numel())
         bytes_ = (active * shape.expert_bytes + tokens * shape.hidden * 2 * 2
                   + tokens * shape.num_experts * 4)
         achieved = bytes_ / (ms / 1e3) / 1e9
         results.append({"tokens": tokens, "ms": round(ms, 5),
+                        "ms_dirty_l2": round(ms_dirty, 5),
                         "tokens_per_s": round(tokens / (ms / 1e3), 1),
                         "active_experts": active, "algorithmic_bytes": bytes_,
                         "achieved_gbs": round(achieved, 1),
@@ -399,7 +411,7 @@ def decode_sweep(steps: int, warmup: int, pk: dict) -> list[dict]:
                                    else "tcgen05-swap" if tokens * shape.top_k <= 4096
                                    else "tcgen05-wide")})
         del graph
-    del layer, flush
+    del layer, flush, flush_read
     torch.cuda.empty_cache()
     return results
 

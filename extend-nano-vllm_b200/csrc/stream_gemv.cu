@@ -409,10 +409,24 @@ __global__ void __launch_bounds__(512) tiny_down_combine_kernel(
   // Routing reads only the logits, which were complete before the gate/up
   // kernel triggered this launch: warm L2 with this CTA's weight rows while
   // the gate/up kernel still runs, then wait for its activations.
-  if (le >= 0 && lane == 0) {
-    const int nrows = min(kTinyDownRows, hidden - h0);
-    prefetch_l2_bulk(w2 + (static_cast<int64_t>(le) * hidden + h0) * inter,
-                     static_cast<uint32_t>(nrows) * inter * 2);
+  if (le >= 0 && lane == 0 && kTinyDownRows > RB) {
+    const int nrows = min(kTinyDownRows - RB, hidden - h0 - RB);
+    if (nrows > 0)
+      prefetch_l2_bulk(w2 + (static_cast<int64_t>(le) * hidden + h0 + RB) * inter,
+                       static_cast<uint32_t>(nrows) * inter * 2);
+  }
+  // The first RB weight rows go to registers before the wait (the weights are
+  // not written by the gate/up kernel); the rest were prefetched into L2.
+  const __nv_bfloat16 *w_exp = w2 + static_cast<int64_t>(le < 0 ? 0 : le) * hidden * inter;
+  uint4 w_first[RB][VPL];
+  if (le >= 0) {
+#pragma unroll
+    for (int r = 0; r < RB; ++r) {
+      const int h = h0 + r;
+      if (h < hidden)
+        load_row<VPL>(reinterpret_cast<const uint4 *>(w_exp + static_cast<int64_t>(h) * inter), V,
+                      lane, w_first[r]);
+    }
   }
   pdl_wait();
   if (le >= 0) {
@@ -422,16 +436,22 @@ __global__ void __launch_bounds__(512) tiny_down_combine_kernel(
   }
   __syncwarp();
   if (le >= 0) {
-    const __nv_bfloat16 *w_exp = w2 + static_cast<int64_t>(le) * hidden * inter;
 #pragma unroll
     for (int f0 = 0; f0 < kTinyDownRows; f0 += RB) {
       uint4 w[RB][VPL];
+      if (f0 == 0) {
 #pragma unroll
-      for (int r = 0; r < RB; ++r) {
-        const int h = h0 + f0 + r;
-        if (h < hidden)
-          load_row<VPL>(reinterpret_cast<const uint4 *>(w_exp + static_cast<int64_t>(h) * inter),
-                        V, lane, w[r]);
+        for (int r = 0; r < RB; ++r)
+#pragma unroll
+          for (int i = 0; i < VPL; ++i) w[r][i] = w_first[r][i];
+      } else {
+#pragma unroll
+        for (int r = 0; r < RB; ++r) {
+          const int h = h0 + f0 + r;
+          if (h < hidden)
+            load_row<VPL>(reinterpret_cast<const uint4 *>(w_exp + static_cast<int64_t>(h) * inter),
+                          V, lane, w[r]);
+        }
       }
 #pragma unroll
       for (int r = 0; r < RB; ++r) {
