@@ -308,3 +308,36 @@ def test_tiny_decode_path_graph_replay():
     assert torch.equal(output, expected_second)
     layer.expert_engine = "stream"
     assert torch.equal(layer(second), expected_second)
+
+
+@torch.inference_mode()
+def test_empty_batch_through_layer_and_every_entry_point():
+    """A step with no tokens (an idle data-parallel rank) returns empty outputs
+    through the layer on every engine and through each C-ABI call, with no
+    kernel error and no device status bit."""
+    from extend_nano_vllm_b200 import ops
+
+    layer, *_ = make_layer(SMALL, 91)
+    x = torch.empty((0, SMALL.hidden), device=DEV, dtype=torch.bfloat16)
+    for engine in ("auto", "stream", "tcgen05-wide", "tcgen05-swap", "tcgen05-pair"):
+        layer.expert_engine = engine
+        out = layer(x)
+        assert out.shape == (0, SMALL.hidden) and out.dtype == torch.bfloat16
+    layer.expert_engine = "auto"
+    logits = torch.empty((0, SMALL.num_experts), device=DEV)
+    w, ids = ops.route_topk(logits, SMALL.top_k, True)
+    assert w.shape == (0, SMALL.top_k) and ids.shape == (0, SMALL.top_k)
+    packed = ops.pack_routes(ids, w.view(-1), SMALL.num_experts, SMALL.num_experts)
+    assert packed.counters.cpu().tolist() == [0] * _lib.NUM_COUNTERS
+    assert packed.expert_offsets.cpu().tolist() == [0] * (SMALL.num_experts + 1)
+    for engine in (_lib.ENGINE_STREAM, _lib.ENGINE_TCGEN05_WIDE, _lib.ENGINE_TCGEN05_SWAP,
+                   _lib.ENGINE_TCGEN05_PAIR):
+        act = ops.expert_gate_up(engine, x, None, layer.gate_up_proj, packed, SMALL.top_k)
+        y = ops.expert_down(engine, act, layer.down_proj, packed, w.view(-1))
+        assert act.shape[0] == packed.row_capacity and y.shape == (0, SMALL.hidden)
+    assert ops.combine(torch.empty((0, SMALL.hidden), device=DEV, dtype=torch.bfloat16),
+                       None, 0, SMALL.top_k).shape == (0, SMALL.hidden)
+    tiny = ops.decode_tiny(logits, x, layer.gate_up_proj, layer.down_proj, SMALL.top_k, True,
+                           SMALL.num_experts)
+    assert tiny.shape == (0, SMALL.hidden)
+    torch.cuda.synchronize()
