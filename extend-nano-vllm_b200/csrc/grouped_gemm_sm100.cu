@@ -33,7 +33,8 @@ namespace tcg {
 constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int A_BYTES = BM * BK * 2;
-constexpr int THREADS = 192;
+constexpr int EPI_GROUPS = 2;                 // epilogue warp groups (4 warps each)
+constexpr int THREADS = 64 + 128 * EPI_GROUPS;  // producer, MMA, epilogue
 
 // Tile configuration for an N tile of BN columns (BN in {64, 128, 256}).
 template <int BN>
@@ -134,7 +135,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(smem_u32(&acc_full[a]), 1);
-      mbar_init(smem_u32(&acc_empty[a]), 4);
+      mbar_init(smem_u32(&acc_empty[a]), 4 * EPI_GROUPS);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -248,8 +249,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
   } else {
-    // ---------------- epilogue (warps 2..5) ----------------
+    // ---------------- epilogue (warps 2..) ----------------
+    // Each TMEM lane quarter is read by one warp of every group; group g
+    // takes the g-th share of the accumulator's columns.
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int grp = (warp - 2) >> 2;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int w = blockIdx.x; w < num_work; w += gridDim.x) {
@@ -266,8 +270,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (kGateUp) {
         const int col0 = n * (BN / 2);
         __nv_bfloat16 *dst_row = args.out + static_cast<int64_t>(row) * args.n_out;
+        constexpr int kGuCols = BN / 2 / EPI_GROUPS;
 #pragma unroll 1
-        for (int c = 0; c < BN / 2; c += 16) {
+        for (int c = grp * kGuCols; c < (grp + 1) * kGuCols; c += 16) {
           float g[16], u[16];
           tmem_ld16(taddr + c, g);
           tmem_ld16(taddr + BN / 2 + c, u);
@@ -306,17 +311,19 @@ __global__ void __launch_bounds__(THREADS, 1)
   } while (0)
         // Two chunks in flight: the next chunk's TMEM load overlaps the
         // scaling and stores of the current one.
+        constexpr int kDnCols = BN / EPI_GROUPS;  // a multiple of 32
+        const int c_begin = grp * kDnCols, c_end = c_begin + kDnCols;
         float va[16], vb[16];
-        tmem_ld16(taddr, va);
+        tmem_ld16(taddr + c_begin, va);
         tmem_wait_into(va);
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = c_begin; c < c_end; c += 32) {
           tmem_ld16(taddr + c + 16, vb);
           B200_EMIT_DOWN(va, c);
           tmem_wait_into(vb);
-          if (c + 32 < BN) tmem_ld16(taddr + c + 32, va);
+          if (c + 32 < c_end) tmem_ld16(taddr + c + 32, va);
           B200_EMIT_DOWN(vb, c + 16);
-          if (c + 32 < BN) tmem_wait_into(va);
+          if (c + 32 < c_end) tmem_wait_into(va);
         }
 #undef B200_EMIT_DOWN
       }
