@@ -36,7 +36,7 @@ constexpr int A_BYTES = BM * BK * 2;
 constexpr int EPI_GROUPS = 2;                 // epilogue warp groups (4 warps each)
 constexpr int THREADS = 64 + 128 * EPI_GROUPS;  // producer, MMA, epilogue
 
-// Tile configuration for an N tile of BN columns (BN in {64, 128, 256}).
+// Tile configuration for an N tile of BN columns (BN in {128, 256}).
 template <int BN>
 struct Cfg {
   static constexpr int B_BYTES = BN * BK * 2;
@@ -46,6 +46,16 @@ struct Cfg {
   static constexpr int TMEM_COLS = 2 * BN;  // two accumulators
   static constexpr size_t SMEM_BYTES = 1024 + static_cast<size_t>(STAGES) * STAGE_BYTES + 256;
 };
+
+// Down epilogue staging: per epilogue warp, 32 rows x 64 bf16 columns (4 KB),
+// so that each global store instruction writes four whole 128-byte row
+// segments instead of 32 scattered 16-byte pieces.
+constexpr int EPI_STAGE_WARP_BYTES = 32 * 64 * 2;
+template <bool kGateUp, int BN>
+constexpr size_t kernel_smem_bytes() {
+  return Cfg<BN>::SMEM_BYTES +
+         (kGateUp ? 0 : static_cast<size_t>(4 * EPI_GROUPS) * EPI_STAGE_WARP_BYTES);
+}
 
 struct Args {
   const int32_t *mtiles;
@@ -123,6 +133,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t *acc_empty = bars + 2 * STAGES + 2;
   uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 4);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+  // Down epilogue staging (kernel_smem_bytes reserves it for the down kernel).
+  uint8_t *epi_stage = smem + STAGES * STAGE_BYTES + 256;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -299,33 +311,53 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
         const int col0 = n * BN;
-        __nv_bfloat16 *dst_row =
-            args.out + static_cast<int64_t>(route < 0 ? 0 : route) * args.n_out;
-#define B200_EMIT_DOWN(V, C)                                                   \
-  do {                                                                         \
-    const int cols = args.n_out - (col0 + (C));                                \
-    if (route >= 0 && cols > 0) {                                              \
-      _Pragma("unroll") for (int i = 0; i < 16; ++i) V[i] *= rw;               \
-      store16_bf16(dst_row + col0 + (C), V, cols);                             \
-    }                                                                          \
-  } while (0)
-        // Two chunks in flight: the next chunk's TMEM load overlaps the
-        // scaling and stores of the current one.
-        constexpr int kDnCols = BN / EPI_GROUPS;  // a multiple of 32
+        // 64 columns at a time: scaled, rounded to bf16 and written to this
+        // warp's staging rows (16-byte slot j of row l at j ^ (l & 7), so
+        // neither the writes nor the reads conflict on banks), then stored
+        // four rows per instruction, eight lanes per 128-byte row segment.
+        uint4 *stage_w = reinterpret_cast<uint4 *>(epi_stage + (warp - 2) * EPI_STAGE_WARP_BYTES);
+        constexpr int kDnCols = BN / EPI_GROUPS;  // a multiple of 64
+        static_assert(kDnCols % 64 == 0, "down epilogue works on 64-column chunks");
         const int c_begin = grp * kDnCols, c_end = c_begin + kDnCols;
-        float va[16], vb[16];
-        tmem_ld16(taddr + c_begin, va);
-        tmem_wait_into(va);
 #pragma unroll 1
-        for (int c = c_begin; c < c_end; c += 32) {
-          tmem_ld16(taddr + c + 16, vb);
-          B200_EMIT_DOWN(va, c);
-          tmem_wait_into(vb);
-          if (c + 32 < c_end) tmem_ld16(taddr + c + 32, va);
-          B200_EMIT_DOWN(vb, c + 16);
-          if (c + 32 < c_end) tmem_wait_into(va);
+        for (int c = c_begin; c < c_end; c += 64) {
+          float v0[16], v1[16], v2[16], v3[16];
+          tmem_ld16(taddr + c, v0);
+          tmem_ld16(taddr + c + 16, v1);
+          tmem_ld16(taddr + c + 32, v2);
+          tmem_ld16(taddr + c + 48, v3);
+          tmem_wait_into(v0);
+          tie16(v1);
+          tie16(v2);
+          tie16(v3);
+#define B200_STAGE_DOWN(V, J)                                                             \
+  do {                                                                                    \
+    uint4 o[2];                                                                           \
+    __nv_bfloat162 *op = reinterpret_cast<__nv_bfloat162 *>(o);                           \
+    _Pragma("unroll") for (int i = 0; i < 8; ++i)                                         \
+        op[i] = __floats2bfloat162_rn(V[2 * i] * rw, V[2 * i + 1] * rw);                  \
+    stage_w[lane * 8 + ((J) ^ (lane & 7))] = o[0];                                        \
+    stage_w[lane * 8 + (((J) + 1) ^ (lane & 7))] = o[1];                                  \
+  } while (0)
+          B200_STAGE_DOWN(v0, 0);
+          B200_STAGE_DOWN(v1, 2);
+          B200_STAGE_DOWN(v2, 4);
+          B200_STAGE_DOWN(v3, 6);
+#undef B200_STAGE_DOWN
+          __syncwarp();
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            const int r = it * 4 + (lane >> 3);
+            const int sl = lane & 7;
+            const int r_route = __shfl_sync(0xffffffffu, route, r);
+            const uint4 o = stage_w[r * 8 + (sl ^ (r & 7))];
+            const int col = col0 + c + sl * 8;
+            if (r_route >= 0 && col < args.n_out)
+              *reinterpret_cast<uint4 *>(args.out + static_cast<int64_t>(r_route) * args.n_out +
+                                         col) = o;
+          }
+          __syncwarp();
         }
-#undef B200_EMIT_DOWN
       }
       tc_fence_before();
       __syncwarp();
@@ -398,7 +430,7 @@ int prepare_kernel() {
   if (dev >= 0 && dev < 64 && done[dev]) return B200MOE_OK;
   B200_CUDA(cudaFuncSetAttribute(grouped_gemm_kernel<kGateUp, BN>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(Cfg<BN>::SMEM_BYTES)));
+                                 static_cast<int>(kernel_smem_bytes<kGateUp, BN>())));
   if (dev >= 0 && dev < 64) done[dev] = true;
   return B200MOE_OK;
 }
@@ -411,7 +443,8 @@ int launch(const CUtensorMap &ma, const CUtensorMap &mb, const Args &args, cudaS
   int grid = sm_count();
   if (work < grid) grid = static_cast<int>(work);
   if (grid < 1) grid = 1;
-  B200_LAUNCH_PDL(kPdlTcgen05, grouped_gemm_kernel<kGateUp, BN>, dim3(grid), dim3(THREADS), Cfg<BN>::SMEM_BYTES, s,
+  B200_LAUNCH_PDL(kPdlTcgen05, grouped_gemm_kernel<kGateUp, BN>, dim3(grid), dim3(THREADS),
+                  kernel_smem_bytes<kGateUp, BN>(), s,
                   ma, mb, args);
   B200_LAUNCHED();
   return B200MOE_OK;
@@ -512,11 +545,9 @@ int tc_gate_up(const RowSource &src, int hidden, int inter, const void *w13, int
       return tc_gate_up_bn<256>(src, hidden, inter, w13, num_local, row_capacity, mtiles,
                                 max_mtiles, counters, act, s);
     case 128:
+    default:
       return tc_gate_up_bn<128>(src, hidden, inter, w13, num_local, row_capacity, mtiles,
                                 max_mtiles, counters, act, s);
-    default:
-      return tc_gate_up_bn<64>(src, hidden, inter, w13, num_local, row_capacity, mtiles,
-                               max_mtiles, counters, act, s);
   }
 }
 
@@ -529,11 +560,9 @@ int tc_down(const void *act, int hidden, int inter, const void *w2, int num_loca
       return tc_down_bn<256>(act, hidden, inter, w2, num_local, row_route, route_weights,
                              num_routes, row_capacity, mtiles, max_mtiles, counters, y, s);
     case 128:
+    default:
       return tc_down_bn<128>(act, hidden, inter, w2, num_local, row_route, route_weights,
                              num_routes, row_capacity, mtiles, max_mtiles, counters, y, s);
-    default:
-      return tc_down_bn<64>(act, hidden, inter, w2, num_local, row_route, route_weights,
-                            num_routes, row_capacity, mtiles, max_mtiles, counters, y, s);
   }
 }
 
