@@ -53,9 +53,9 @@ __device__ __forceinline__ void store8<double, double>(double *dst, const double
 
 // One thread per 8 columns of one token.  hidden % 8 == 0.
 // kBatch (small batches, latency-bound): the slot rows of eight routes are
-// requested together before any is summed; otherwise one slot at a time
-// (bandwidth-bound batches keep more threads resident).  The sum is in slot
-// order either way.
+// requested together before any is summed; otherwise four at a time (fewer
+// registers, so bandwidth-bound batches keep more threads resident).  The sum
+// is in slot order either way.
 template <typename Acc, typename Out, bool kBatch>
 __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16 *y,
                                                       int64_t num_rows,
@@ -100,10 +100,24 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16 *y,
         if (row[j] >= 0 && row[j] < num_rows) add(v[j]);
     }
   } else {
-    for (int s = 0; s < top_k; ++s) {
-      const int64_t route = token * top_k + s;
-      const int64_t row = route_rows ? static_cast<int64_t>(route_rows[route]) : route;
-      if (row >= 0 && row < num_rows) add(*reinterpret_cast<const uint4 *>(y + row * hidden + col));
+    // Four slots per step: their row indices, then their rows, are requested
+    // together (two round trips per four slots instead of eight).
+    for (int s0 = 0; s0 < top_k; s0 += 4) {
+      int64_t row[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int64_t route = token * top_k + s0 + j;
+        row[j] = s0 + j >= top_k ? -1
+                 : (route_rows ? static_cast<int64_t>(route_rows[route]) : route);
+      }
+      uint4 v[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (row[j] >= 0 && row[j] < num_rows)
+          v[j] = *reinterpret_cast<const uint4 *>(y + row[j] * hidden + col);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (row[j] >= 0 && row[j] < num_rows) add(v[j]);
     }
   }
   store8<Acc, Out>(out + token * hidden + col, acc);
