@@ -17,6 +17,8 @@
 //  2. pack_scatter: every block prefixes the histograms of the blocks before
 //                   it, recomputes the local-expert layout, then ranks its own
 //                   routes in order (warp match + per-warp counts) and scatters.
+// With a single route block (up to 1024 routes: decode buckets) pack_scatter
+// does pack_hist's work itself and pack_hist is not launched.
 #include "common.cuh"
 
 namespace b200moe {
@@ -102,6 +104,10 @@ struct ScatterArgs {
   const int32_t *hist;
   int64_t chunk;
   int nblk;
+  // One route block (nblk == 1): the scatter kernel also does the pack_hist
+  // work (its histogram, the sentinel fills, zeroed counters), one launch
+  // instead of two.
+  int single;
 };
 
 // Shared memory (int32 words): base[E1] tot[E1] run[E1] loc[E1]
@@ -136,16 +142,32 @@ __global__ void __launch_bounds__(kPackThreads) pack_scatter_kernel(ScatterArgs 
   for (int i = tid; i < L; i += blockDim.x) gof[i] = -1;
   if (tid < 5) red[tid] = 0;
   for (int i = tid; i < kPackWarps * E1; i += blockDim.x) warp_cnt[i] = 0;
+  if (a.single) {
+    // pack_hist's work for the only block: histogram into tot, sentinels.
+    for (int e = tid; e < E1; e += blockDim.x) tot[e] = 0;
+    const int32_t sentinel = static_cast<int32_t>(a.num_routes);
+    for (int64_t i = tid; i < a.row_capacity; i += blockDim.x) a.row_route[i] = sentinel;
+    for (int64_t i = tid; i < a.row_capacity / B200MOE_BLOCK_ROWS; i += blockDim.x)
+      a.tile_expert[i] = 0;
+    if (tid < B200MOE_NUM_COUNTERS) a.counters[tid] = 0;
+    __syncthreads();
+    for (int64_t r = tid; r < a.num_routes; r += blockDim.x)
+      atomicAdd(&tot[route_key(a.ids[r], E)], 1);
+  }
   __syncthreads();
   for (int e = tid; e < E1; e += blockDim.x) {
     int32_t before = 0, all = 0;
-    // Independent loads: unrolled so several are in flight (this prefix over
-    // the blocks' histograms is the scatter kernel's critical path).
+    if (a.single) {
+      all = tot[e];
+    } else {
+      // Independent loads: unrolled so several are in flight (this prefix
+      // over the blocks' histograms is the scatter kernel's critical path).
 #pragma unroll 8
-    for (int bb = 0; bb < a.nblk; ++bb) {
-      const int32_t h = a.hist[static_cast<int64_t>(bb) * E1 + e];
-      if (bb < b) before += h;
-      all += h;
+      for (int bb = 0; bb < a.nblk; ++bb) {
+        const int32_t h = a.hist[static_cast<int64_t>(bb) * E1 + e];
+        if (bb < b) before += h;
+        all += h;
+      }
     }
     base[e] = before;
     tot[e] = all;
@@ -413,11 +435,14 @@ int b200moe_pack_routes(int64_t *expert_ids, void *route_weights, int64_t num_ro
   B200_ARG(scratch != nullptr && scratch_bytes >= need, "scratch needs %zu bytes", need);
   int32_t *hist = static_cast<int32_t *>(scratch);
 
-  const size_t hist_smem = sizeof(int32_t) * (num_experts + 1);
-  B200_LAUNCH_PDL(kPdlPack, pack_hist_kernel, dim3(g.nblk), dim3(kPackThreads), hist_smem, s,
-      expert_ids, num_routes, num_experts, g.chunk, hist, row_route, row_capacity, tile_expert,
-      counters);
-  B200_LAUNCHED();
+  const bool single = g.nblk == 1;
+  if (!single) {
+    const size_t hist_smem = sizeof(int32_t) * (num_experts + 1);
+    B200_LAUNCH_PDL(kPdlPack, pack_hist_kernel, dim3(g.nblk), dim3(kPackThreads), hist_smem, s,
+        expert_ids, num_routes, num_experts, g.chunk, hist, row_route, row_capacity, tile_expert,
+        counters);
+    B200_LAUNCHED();
+  }
 
   ScatterArgs a;
   a.ids = expert_ids;
@@ -444,6 +469,7 @@ int b200moe_pack_routes(int64_t *expert_ids, void *route_weights, int64_t num_ro
   a.hist = hist;
   a.chunk = g.chunk;
   a.nblk = g.nblk;
+  a.single = single ? 1 : 0;
   const size_t smem = scatter_smem_bytes(num_experts, num_local_experts);
   if (smem > 48 * 1024) {
     B200_CUDA(cudaFuncSetAttribute(pack_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
