@@ -39,7 +39,8 @@ constexpr int BOX_ROWS = 16;
 constexpr int W_BYTES = FM * BK * 2;
 constexpr int X_BYTES = NMAX * BK * 2;
 constexpr int BOX_BYTES = BOX_ROWS * BK * 2;
-constexpr int THREADS = 192;
+constexpr int EPI_GROUPS = 2;                 // epilogue warp groups (4 warps each)
+constexpr int THREADS = 64 + 128 * EPI_GROUPS;  // producer, MMA, epilogue
 
 template <bool kGateUp>
 struct Cfg {
@@ -71,7 +72,7 @@ struct Args {
 };
 
 __device__ __forceinline__ void epi_bar() {
-  asm volatile("bar.sync 1, 128;" ::: "memory");
+  asm volatile("bar.sync 1, %0;" ::"n"(128 * EPI_GROUPS) : "memory");
 }
 
 template <bool kGateUp>
@@ -105,7 +106,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(smem_u32(&acc_full[a]), 1);
-      mbar_init(smem_u32(&acc_empty[a]), 4);
+      mbar_init(smem_u32(&acc_empty[a]), 4 * EPI_GROUPS);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -232,9 +233,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
   } else {
-    // ---------------- epilogue (warps 2..5) ----------------
+    // ---------------- epilogue (warps 2..) ----------------
     const int q = warp & 3;  // TMEM lane quarter = 32 features
-    const int et = threadIdx.x - 64;  // 0..127 among epilogue threads
+    const int et = threadIdx.x - 64;  // index among the epilogue threads
+    const int grp = (warp - 2) >> 2;  // group g takes column chunks g, g + G, ...
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int w = blockIdx.x; w < num_work; w += gridDim.x) {
@@ -265,7 +267,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                              static_cast<uint32_t>(acc * C::ACC_COLS);
 #pragma unroll 1
-      for (int c = 0; c < n_mma; c += 16) {
+      for (int c = 16 * grp; c < n_mma; c += 16 * EPI_GROUPS) {
         if (kGateUp) {
           float g[16], u[16];
           tmem_ld16(taddr + c, g);
