@@ -61,7 +61,24 @@ SIGNATURES: dict[str, tuple] = {
     "b200moe_ep_pack": (_I, [_P, _I, _P, _P, _L, _I, _I, _P, _I, _P, _P, _P, _P, _P, _P, _P]),
     "b200moe_ep_unpack_routes": (_I, [_P, _L, _I, _P, _P, _P, _P, _P, _P, _P]),
     "b200moe_ep_return_rows": (_I, [_P, _P, _L, _I, _I, _P, _P, _L, _P, _P]),
+    "b200moe_pack_routes_device_bounds": (_I, [_P, _P, _L, _P, _I, _P, _I, _I, _P, _L, _P, _L,
+                                               _P, _P, _P, _P, _P, _P, _P, _L, _P, _P, _P, _P,
+                                               _S, _P]),
+    "b200moe_nvl_buffer_bytes": (_L, [_I, _L, _I, _I, _I, _I, _P]),
+    "b200moe_ipc_handle": (_I, [_P, _P, _P]),
+    "b200moe_ipc_open": (_I, [_P, _L, _P]),
+    "b200moe_ipc_close": (_I, [_P, _L]),
+    "b200moe_nvl_histogram_send": (_I, [_P, _L, _I, _I, _I, _I, _P, _P, _P]),
+    "b200moe_nvl_histogram_wait": (_I, [_I, _I, _I, _I, _P, _P, ctypes.c_double, _P, _P, _P,
+                                        _P]),
+    "b200moe_nvl_dispatch": (_I, [_P, _I, _P, _P, _L, _I, _I, _P, _I, _I, _P, _P, _P, _P, _P, _L,
+                                  _I, _P, _P]),
+    "b200moe_nvl_receive": (_I, [_I, _I, _P, _P, _L, _P, _P, _P, _P, _P, _P, _P]),
+    "b200moe_nvl_return": (_I, [_P, _I, _P, _P, _P, _L, _L, _I, _I, _P, _P, _P]),
+    "b200moe_nvl_wait_return": (_I, [_I, _I, _P, _P, _P]),
 }
+NVL_LAYOUT_WORDS = 10
+NVL_ROUTE_CAP = 8  # layout word: route records per source region
 
 
 class B200MoEError(RuntimeError):
@@ -90,27 +107,43 @@ def _load() -> ctypes.CDLL:
 LIB = _load()
 
 
-# Kernels each entry point launches (for launch accounting; the streaming
-# and tcgen05 engines both launch one kernel per projection).
-KERNELS_PER_CALL = {"b200moe_pack_routes": 2, "b200moe_pack_routes_static_scratch": 2,
-                    "b200moe_decode_tiny": 2}
-# Calls made through call(), by entry-point name (launch accounting).
+# Largest route count the packing call handles with one kernel (one route
+# block: the scatter kernel builds its own histogram); above it, two.
+PACK_SINGLE_LAUNCH_ROUTES = 1024
+# Calls made through call(), by entry-point name, and the kernels they
+# launched (launch accounting; the streaming and tcgen05 engines launch one
+# kernel per projection, the tiny decode path two).
 CALL_COUNTS: dict[str, int] = {}
+LAUNCH_COUNTS: dict[str, int] = {}
+_NO_KERNEL = ("b200moe_device_status", "b200moe_ipc_handle", "b200moe_ipc_open",
+              "b200moe_ipc_close")
+
+
+def _kernels_launched(name: str, args: tuple) -> int:
+    if name in _NO_KERNEL:
+        return 0
+    if name in ("b200moe_pack_routes", "b200moe_pack_routes_static_scratch"):
+        routes = int(args[2])
+        return 0 if routes == 0 else 1 if routes <= PACK_SINGLE_LAUNCH_ROUTES else 2
+    if name == "b200moe_decode_tiny":
+        return 2 if int(args[3]) > 0 else 0
+    if name == "b200moe_pack_routes_device_bounds":
+        return 1 if int(args[2]) <= PACK_SINGLE_LAUNCH_ROUTES else 2
+    if name == "b200moe_nvl_receive":
+        return 2
+    return 1
 
 
 def launches_since(snapshot: dict[str, int]) -> int:
-    """Kernels launched by library calls made after ``snapshot`` was taken."""
-    total = 0
-    for name, count in CALL_COUNTS.items():
-        if name.startswith("b200moe_device_status"):
-            continue
-        total += (count - snapshot.get(name, 0)) * KERNELS_PER_CALL.get(name, 1)
-    return total
+    """Kernels launched by library calls made after ``snapshot`` (a copy of
+    LAUNCH_COUNTS) was taken."""
+    return sum(count - snapshot.get(name, 0) for name, count in LAUNCH_COUNTS.items())
 
 
 def call(name: str, *args) -> None:
     """Call an int-returning entry point and raise on a non-zero status."""
     CALL_COUNTS[name] = CALL_COUNTS.get(name, 0) + 1
+    LAUNCH_COUNTS[name] = LAUNCH_COUNTS.get(name, 0) + _kernels_launched(name, args)
     rc = getattr(LIB, name)(*args)
     if rc != OK:
         message = LIB.b200moe_last_error().decode(errors="replace")

@@ -27,6 +27,7 @@ enum PdlFamily : unsigned {
   kPdlStream = 16u,
   kPdlTiny = 32u,
   kPdlTcgen05 = 64u,
+  kPdlExchange = 128u,
 };
 bool pdl_enabled(unsigned family);
 // Device-side sticky status word (bit 0: bounded wait gave up, bit 1: index

@@ -54,10 +54,16 @@ __device__ __forceinline__ int route_key(int64_t id, int num_experts) {
   return (id >= 0 && id < num_experts) ? static_cast<int>(id) : num_experts;
 }
 
+// Routes the packing kernels process: num_routes, or fewer when the caller
+// gives a device-side count (routes at or above it are left untouched).
+__device__ __forceinline__ int64_t routes_in_use(int64_t num_routes, const int32_t *route_count) {
+  return route_count ? min64(num_routes, max64(0, *route_count)) : num_routes;
+}
+
 __global__ void __launch_bounds__(kPackThreads) pack_hist_kernel(
-    const int64_t *ids, int64_t num_routes, int num_experts, int64_t chunk,
-    int32_t *__restrict__ hist, int32_t *__restrict__ row_route, int64_t row_capacity,
-    int32_t *__restrict__ tile_expert, int32_t *__restrict__ counters) {
+    const int64_t *ids, int64_t num_routes, const int32_t *route_count, int num_experts,
+    int64_t chunk, int32_t *__restrict__ hist, int32_t *__restrict__ row_route,
+    int64_t row_capacity, int32_t *__restrict__ tile_expert, int32_t *__restrict__ counters) {
   pdl_trigger();
   pdl_wait();
   extern __shared__ int32_t sh_hist[];
@@ -65,7 +71,7 @@ __global__ void __launch_bounds__(kPackThreads) pack_hist_kernel(
   for (int e = threadIdx.x; e < E1; e += blockDim.x) sh_hist[e] = 0;
   __syncthreads();
   const int64_t begin = blockIdx.x * chunk;
-  const int64_t end = min(num_routes, begin + chunk);
+  const int64_t end = min(routes_in_use(num_routes, route_count), begin + chunk);
   for (int64_t r = begin + threadIdx.x; r < end; r += blockDim.x)
     atomicAdd(&sh_hist[route_key(ids[r], num_experts)], 1);
   __syncthreads();
@@ -89,6 +95,8 @@ struct ScatterArgs {
   int num_local;
   const int32_t *expert_base;
   int64_t capacity;  // < 0: unlimited
+  const int64_t *capacity_dev;  // device-side capacity (overrides capacity) or null
+  const int32_t *route_count;   // device-side number of routes in use, or null
   int64_t row_capacity;
   int32_t *row_route;
   int32_t *route_row;
@@ -137,7 +145,9 @@ __global__ void __launch_bounds__(kPackThreads) pack_scatter_kernel(ScatterArgs 
   const int lane = tid & 31;
   const int warp = tid >> 5;
   const int b = blockIdx.x;
-  const int64_t cap = a.capacity < 0 ? (int64_t)0x3fffffffffffffffLL : a.capacity;
+  const int64_t cap_value = a.capacity_dev ? *a.capacity_dev : a.capacity;
+  const int64_t cap = cap_value < 0 ? (int64_t)0x3fffffffffffffffLL : cap_value;
+  const int64_t n_routes = routes_in_use(a.num_routes, a.route_count);
 
   for (int i = tid; i < L; i += blockDim.x) gof[i] = -1;
   if (tid < 5) red[tid] = 0;
@@ -151,7 +161,7 @@ __global__ void __launch_bounds__(kPackThreads) pack_scatter_kernel(ScatterArgs 
       a.tile_expert[i] = 0;
     if (tid < B200MOE_NUM_COUNTERS) a.counters[tid] = 0;
     __syncthreads();
-    for (int64_t r = tid; r < a.num_routes; r += blockDim.x)
+    for (int64_t r = tid; r < n_routes; r += blockDim.x)
       atomicAdd(&tot[route_key(a.ids[r], E)], 1);
   }
   __syncthreads();
@@ -288,7 +298,7 @@ __global__ void __launch_bounds__(kPackThreads) pack_scatter_kernel(ScatterArgs 
 
   // Rank this block's routes in order and scatter.
   const int64_t begin = static_cast<int64_t>(b) * a.chunk;
-  const int64_t end = min(a.num_routes, begin + a.chunk);
+  const int64_t end = min(n_routes, begin + a.chunk);
   int my_kept = 0, my_dropped = 0;
   const int32_t route_sentinel = static_cast<int32_t>(a.num_routes);
   const int32_t row_sentinel = static_cast<int32_t>(a.row_capacity);
@@ -385,32 +395,15 @@ size_t scatter_smem_bytes(int num_experts, int num_local) {
 }  // namespace
 }  // namespace b200moe
 
-extern "C" {
-
-int64_t b200moe_pack_row_capacity(int64_t num_routes, int num_local_experts) {
-  const int64_t active = num_routes < num_local_experts ? num_routes : num_local_experts;
-  const int64_t rows = num_routes + active * (B200MOE_BLOCK_ROWS - 1);
-  return (rows + B200MOE_BLOCK_ROWS - 1) / B200MOE_BLOCK_ROWS * B200MOE_BLOCK_ROWS;
-}
-
-int64_t b200moe_pack_max_mtiles(int64_t num_routes, int num_local_experts) {
-  const int64_t active = num_routes < num_local_experts ? num_routes : num_local_experts;
-  return (num_routes + B200MOE_MTILE_ROWS - 1) / B200MOE_MTILE_ROWS + active;
-}
-
-size_t b200moe_pack_scratch_bytes(int64_t num_routes, int num_experts) {
-  const auto g = b200moe::pack_geometry(num_routes);
-  return static_cast<size_t>(g.nblk) * (static_cast<size_t>(num_experts) + 1) * sizeof(int32_t);
-}
-
-int b200moe_pack_routes(int64_t *expert_ids, void *route_weights, int64_t num_routes,
-                        int num_experts, const int64_t *local_index, int expert_start,
-                        int num_local_experts, const int32_t *expert_base, int64_t capacity,
-                        int64_t row_capacity, int32_t *row_route, int32_t *route_row,
-                        int32_t *combine_rows, int32_t *tile_expert, int32_t *expert_offsets,
-                        int32_t *expert_counts, int32_t *mtiles, int64_t max_mtiles,
-                        int32_t *chunks, int32_t *counters, int64_t *stats, void *scratch,
-                        size_t scratch_bytes, void *stream) {
+static int pack_routes_impl(int64_t *expert_ids, void *route_weights, int64_t num_routes,
+                            int num_experts, const int64_t *local_index, int expert_start,
+                            int num_local_experts, const int32_t *expert_base, int64_t capacity,
+                            const int64_t *capacity_dev, const int32_t *route_count,
+                            int64_t row_capacity, int32_t *row_route, int32_t *route_row,
+                            int32_t *combine_rows, int32_t *tile_expert, int32_t *expert_offsets,
+                            int32_t *expert_counts, int32_t *mtiles, int64_t max_mtiles,
+                            int32_t *chunks, int32_t *counters, int64_t *stats, void *scratch,
+                            size_t scratch_bytes, void *stream) {
   using namespace b200moe;
   B200_ARG(num_routes >= 0 && num_routes < (int64_t)0x7fffffff, "num_routes out of range");
   B200_ARG(num_experts >= 1 && num_experts <= 4096, "num_experts must be in [1, 4096]");
@@ -439,8 +432,8 @@ int b200moe_pack_routes(int64_t *expert_ids, void *route_weights, int64_t num_ro
   if (!single) {
     const size_t hist_smem = sizeof(int32_t) * (num_experts + 1);
     B200_LAUNCH_PDL(kPdlPack, pack_hist_kernel, dim3(g.nblk), dim3(kPackThreads), hist_smem, s,
-        expert_ids, num_routes, num_experts, g.chunk, hist, row_route, row_capacity, tile_expert,
-        counters);
+        expert_ids, num_routes, route_count, num_experts, g.chunk, hist, row_route, row_capacity,
+        tile_expert, counters);
     B200_LAUNCHED();
   }
 
@@ -454,6 +447,8 @@ int b200moe_pack_routes(int64_t *expert_ids, void *route_weights, int64_t num_ro
   a.num_local = num_local_experts;
   a.expert_base = expert_base;
   a.capacity = capacity;
+  a.capacity_dev = capacity_dev;
+  a.route_count = route_count;
   a.row_capacity = row_capacity;
   a.row_route = row_route;
   a.route_row = route_row;
@@ -478,6 +473,54 @@ int b200moe_pack_routes(int64_t *expert_ids, void *route_weights, int64_t num_ro
   B200_LAUNCH_PDL(kPdlPack, pack_scatter_kernel, dim3(g.nblk), dim3(kPackThreads), smem, s, a);
   B200_LAUNCHED();
   return B200MOE_OK;
+}
+
+extern "C" {
+
+int64_t b200moe_pack_row_capacity(int64_t num_routes, int num_local_experts) {
+  const int64_t active = num_routes < num_local_experts ? num_routes : num_local_experts;
+  const int64_t rows = num_routes + active * (B200MOE_BLOCK_ROWS - 1);
+  return (rows + B200MOE_BLOCK_ROWS - 1) / B200MOE_BLOCK_ROWS * B200MOE_BLOCK_ROWS;
+}
+
+int64_t b200moe_pack_max_mtiles(int64_t num_routes, int num_local_experts) {
+  const int64_t active = num_routes < num_local_experts ? num_routes : num_local_experts;
+  return (num_routes + B200MOE_MTILE_ROWS - 1) / B200MOE_MTILE_ROWS + active;
+}
+
+size_t b200moe_pack_scratch_bytes(int64_t num_routes, int num_experts) {
+  const auto g = b200moe::pack_geometry(num_routes);
+  return static_cast<size_t>(g.nblk) * (static_cast<size_t>(num_experts) + 1) * sizeof(int32_t);
+}
+
+int b200moe_pack_routes(int64_t *expert_ids, void *route_weights, int64_t num_routes,
+                        int num_experts, const int64_t *local_index, int expert_start,
+                        int num_local_experts, const int32_t *expert_base, int64_t capacity,
+                        int64_t row_capacity, int32_t *row_route, int32_t *route_row,
+                        int32_t *combine_rows, int32_t *tile_expert, int32_t *expert_offsets,
+                        int32_t *expert_counts, int32_t *mtiles, int64_t max_mtiles,
+                        int32_t *chunks, int32_t *counters, int64_t *stats, void *scratch,
+                        size_t scratch_bytes, void *stream) {
+  return pack_routes_impl(expert_ids, route_weights, num_routes, num_experts, local_index,
+                          expert_start, num_local_experts, expert_base, capacity, nullptr,
+                          nullptr, row_capacity, row_route, route_row, combine_rows,
+                          tile_expert, expert_offsets, expert_counts, mtiles, max_mtiles, chunks,
+                          counters, stats, scratch, scratch_bytes, stream);
+}
+
+int b200moe_pack_routes_device_bounds(
+    int64_t *expert_ids, void *route_weights, int64_t num_routes, const int32_t *route_count,
+    int num_experts, const int64_t *local_index, int expert_start, int num_local_experts,
+    const int32_t *expert_base, int64_t capacity, const int64_t *capacity_dev,
+    int64_t row_capacity, int32_t *row_route, int32_t *route_row, int32_t *combine_rows,
+    int32_t *tile_expert, int32_t *expert_offsets, int32_t *expert_counts, int32_t *mtiles,
+    int64_t max_mtiles, int32_t *chunks, int32_t *counters, int64_t *stats, void *scratch,
+    size_t scratch_bytes, void *stream) {
+  return pack_routes_impl(expert_ids, route_weights, num_routes, num_experts, local_index,
+                          expert_start, num_local_experts, expert_base, capacity, capacity_dev,
+                          route_count, row_capacity, row_route, route_row, combine_rows,
+                          tile_expert, expert_offsets, expert_counts, mtiles, max_mtiles, chunks,
+                          counters, stats, scratch, scratch_bytes, stream);
 }
 
 int b200moe_expert_histogram(const int64_t *expert_ids, int64_t num_routes, int num_experts,
@@ -521,10 +564,40 @@ static __device__ __align__(256) int32_t g_pack_static_scratch[kPackStaticScratc
 
 std::mutex g_static_scratch_mutex;
 void *g_static_scratch_addr[64] = {nullptr};
+unsigned long long g_static_scratch_ctx[64] = {0};
 
-// Device address of the static array on the current device.  The first call
-// on a device looks it up with cudaGetSymbolAddress (that device current);
-// later calls reuse the cached address.
+// Unique id of the calling thread's current CUDA context (cuCtxGetId, fetched
+// from the driver at run time); false when there is no current context or
+// the driver cannot say.
+bool current_context_id(unsigned long long *id) {
+  using GetCurrent = CUresult (*)(CUcontext *);
+  using GetId = CUresult (*)(CUcontext, unsigned long long *);
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  static bool resolved = false;
+  if (!resolved) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess && q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<GetCurrent>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess && q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetId>(p);
+    resolved = true;
+  }
+  if (get_current == nullptr || get_id == nullptr) return false;
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return false;
+  return get_id(ctx, id) == CUDA_SUCCESS;
+}
+
+// Device address of the static array in the current device's context.  The
+// first call on a device (and the first call after that device's context was
+// destroyed and re-created, e.g. by cudaDeviceReset) looks it up with
+// cudaGetSymbolAddress, that device current; later calls in the same context
+// reuse the address.
 int static_scratch_address(void **out) {
   const int dev = current_device();
   if (dev < 0 || dev >= 64) {
@@ -532,10 +605,17 @@ int static_scratch_address(void **out) {
     return B200MOE_EUNSUPPORTED;
   }
   std::lock_guard<std::mutex> lock(g_static_scratch_mutex);
-  if (g_static_scratch_addr[dev] == nullptr) {
+  unsigned long long ctx = 0;
+  const bool known = current_context_id(&ctx);
+  if (g_static_scratch_addr[dev] == nullptr || !known || ctx != g_static_scratch_ctx[dev]) {
     void *p = nullptr;
     B200_CUDA(cudaGetSymbolAddress(&p, g_pack_static_scratch));
-    g_static_scratch_addr[dev] = p;
+    unsigned long long now = 0;
+    // Without a context id the address is looked up on every call.
+    g_static_scratch_addr[dev] = current_context_id(&now) ? p : nullptr;
+    g_static_scratch_ctx[dev] = now;
+    *out = p;
+    return B200MOE_OK;
   }
   *out = g_static_scratch_addr[dev];
   return B200MOE_OK;

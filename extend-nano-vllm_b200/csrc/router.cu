@@ -4,9 +4,9 @@
 //   probs = F.softmax(logits, dim=-1, dtype=float32)
 //   w, ids = torch.topk(probs, k);  if norm_topk_prob: w /= w.sum(-1)
 //   w = w.to(bf16)
-// Selection ranks experts by descending logit with ties going to the lower
-// index; softmax is monotone so this is the same set and order as top-k over
-// the probabilities wherever the probabilities are distinct.
+// The warp routine (route_warp.cuh) reproduces torch's CUDA softmax, top-k
+// order for equal probabilities and renormalisation sum, so ids and weights
+// equal the reference's GPU routing bit for bit.
 #include "route_warp.cuh"
 
 namespace b200moe {

@@ -12,8 +12,9 @@ CPU or Triton path: CPU tensors raise.
 
 Differences from the reference, by design:
   * an additional dispatch backend ``"all_to_all_nvlink"``: every EP rank
-    routes its own tokens and exchanges tokens/route results with NCCL
-    all-to-all (the reference all-gathers every replica's tokens);
+    routes its own tokens and exchanges token rows and route results with
+    its peers over NVLink peer memory, graph-safe and without host reads
+    under capture (the reference all-gathers every replica's tokens);
   * the unfused grouped-GEMM seam ``_run_grouped_gemm`` does not exist (gate/up
     and SwiGLU are one kernel), nor does the per-expert torch loop
     ``_forward_reference`` (correctness oracles live with the tests);
@@ -235,10 +236,13 @@ class ExpertParallelMoE(nn.Module):
         self.ep_all_to_all_count = 0
         self.ep_broadcast_count = 0
         self.total_assignment_count = 0
-        self.total_dispatch_token_count = 0
+        # Largest batch (tokens per rank) the NVLink exchange buffers hold
+        # ("all_to_all_nvlink"); None: nvl.DEFAULT_MAX_TOKENS.
+        self.nvl_max_tokens: int | None = None
         # Counters fed by kernels: host part + device accumulator
-        # [local kept routes, dropped routes], read (synchronising) on access.
-        self._host_counts = {"dispatch": 0, "return": 0, "dropped": 0}
+        # [local kept routes, dropped routes, dispatched tokens], read
+        # (synchronising) on access.
+        self._host_counts = {"dispatch": 0, "return": 0, "dropped": 0, "tokens": 0}
         self._stats: torch.Tensor | None = None
 
     # ------------------------------------------------------------------
@@ -254,14 +258,23 @@ class ExpertParallelMoE(nn.Module):
             self._host_counts["dispatch"] += previous[0]
             self._host_counts["return"] += previous[0]
             self._host_counts["dropped"] += previous[1]
-            self._stats = torch.zeros(2, device=device, dtype=torch.int64)
+            self._host_counts["tokens"] += previous[2]
+            self._stats = torch.zeros(3, device=device, dtype=torch.int64)
         return self._stats
 
-    def _read_stats(self) -> tuple[int, int]:
+    def _read_stats(self) -> tuple[int, int, int]:
         if self._stats is None:
-            return 0, 0
-        kept, dropped = self._stats.tolist()
-        return int(kept), int(dropped)
+            return 0, 0, 0
+        kept, dropped, tokens = self._stats.tolist()
+        return int(kept), int(dropped), int(tokens)
+
+    @property
+    def total_dispatch_token_count(self) -> int:
+        return self._host_counts["tokens"] + self._read_stats()[2]
+
+    @total_dispatch_token_count.setter
+    def total_dispatch_token_count(self, value: int) -> None:
+        self._host_counts["tokens"] = int(value) - self._read_stats()[2]
 
     @property
     def dispatch_assignment_count(self) -> int:
@@ -425,12 +438,16 @@ class ExpertParallelMoE(nn.Module):
 
     def _pack(self, flat_ids: torch.Tensor, flat_weights: torch.Tensor | None, *,
               capacity: int | None = None, expert_base: torch.Tensor | None = None,
-              stats: torch.Tensor | None = None):
+              stats: torch.Tensor | None = None, route_count: torch.Tensor | None = None,
+              capacity_dev: torch.Tensor | None = None):
         local_index = self.expert_local_index_tensor if self.expert_id_to_local is not None else None
+        bounds = {}
+        if route_count is not None or capacity_dev is not None:
+            bounds = dict(route_count=route_count, capacity_dev=capacity_dev)
         return self._ops.pack_routes(
             flat_ids, flat_weights, self.num_experts, self.num_local_experts,
             local_index=local_index, expert_start=max(self.expert_start, 0),
-            expert_base=expert_base, capacity=capacity, stats=stats)
+            expert_base=expert_base, capacity=capacity, stats=stats, **bounds)
 
     def _use_tiny_path(self, num_tokens: int, logits: torch.Tensor) -> bool:
         """Two-launch fused path: tiny buckets, no capacity, plain bf16 combine."""
@@ -456,13 +473,22 @@ class ExpertParallelMoE(nn.Module):
         return _lib.ENGINE_STREAM if num_routes <= STREAM_ENGINE_MAX_ROUTES else _lib.ENGINE_TCGEN05
 
     def _run_experts(self, x: torch.Tensor, flat_weights: torch.Tensor, packed, top_k: int,
-                     token_of_route: torch.Tensor | None = None) -> torch.Tensor:
-        """Grouped gate/up + SwiGLU and grouped down -> y [num_routes, H] (route order)."""
-        engine = self._engine(packed.num_routes)
+                     token_of_route: torch.Tensor | None = None,
+                     routes_hint: int | None = None) -> torch.Tensor:
+        """Grouped gate/up + SwiGLU and grouped down -> y [num_routes, H] (route order).
+
+        ``routes_hint``: the expected number of routes when ``packed`` is
+        bounded on the device (its host num_routes is then only a maximum);
+        it picks the tcgen05 variant and the row-gather strategy, and the
+        streaming engine (whose route bound is compiled in) is not used."""
+        routes = packed.num_routes if routes_hint is None else max(1, int(routes_hint))
+        engine = self._engine(routes)
+        if routes_hint is not None and engine in (_lib.ENGINE_STREAM, _lib.ENGINE_TCGEN05):
+            engine = (_lib.ENGINE_TCGEN05_SWAP if routes <= 4096 else _lib.ENGINE_TCGEN05_WIDE)
         ops = self._ops
         timer = self.kernel_timer
         if engine == _lib.ENGINE_STREAM or (engine != _lib.ENGINE_TCGEN05_PAIR and
-                                            packed.num_routes <= FUSED_GATHER_MAX_ROUTES):
+                                            routes <= FUSED_GATHER_MAX_ROUTES):
             # The streaming engine reads token rows directly; for small
             # buckets the one-SM tcgen05 engines gather them inside their TMA
             # loads (four rows per tile::gather4), saving the gather launch.

@@ -78,11 +78,14 @@ def pack_routes(expert_ids: torch.Tensor, route_weights: torch.Tensor | None,
                 num_experts: int, num_local_experts: int, *,
                 local_index: torch.Tensor | None = None, expert_start: int = 0,
                 expert_base: torch.Tensor | None = None, capacity: int | None = None,
-                stats: torch.Tensor | None = None) -> PackedRoutes:
+                stats: torch.Tensor | None = None, route_count: torch.Tensor | None = None,
+                capacity_dev: torch.Tensor | None = None) -> PackedRoutes:
     """Capacity + expert-major packing of flat int64 routes.
 
     With ``capacity`` set, dropped routes are rewritten in place in
     ``expert_ids`` (to num_experts) and ``route_weights`` (to 0).
+    ``route_count`` (device int32 [1]) packs only the first routes;
+    ``capacity_dev`` (device int64 [1]) replaces ``capacity``.
     """
     _require_cuda(expert_ids)
     if expert_ids.dtype != torch.int64 or not expert_ids.is_contiguous():
@@ -112,12 +115,25 @@ def pack_routes(expert_ids: torch.Tensor, route_weights: torch.Tensor | None,
     if route_weights is not None and (route_weights.dtype != torch.bfloat16
                                       or route_weights.numel() != routes):
         raise TypeError("route_weights must be bf16 with one weight per route")
-    call("b200moe_pack_routes", _p(flat), _p(route_weights), routes, num_experts,
-         _p(local_index), int(expert_start), num_local_experts, _p(expert_base),
-         -1 if capacity is None else int(capacity), row_capacity, _p(row_route),
-         _p(route_row), _p(combine_rows), _p(tile_expert), _p(expert_offsets),
-         _p(expert_counts), _p(mtiles), max_mtiles, _p(chunks), _p(counters), _p(stats),
-         _p(scratch), scratch.numel() * 4, _stream(flat))
+    if route_count is None and capacity_dev is None:
+        call("b200moe_pack_routes", _p(flat), _p(route_weights), routes, num_experts,
+             _p(local_index), int(expert_start), num_local_experts, _p(expert_base),
+             -1 if capacity is None else int(capacity), row_capacity, _p(row_route),
+             _p(route_row), _p(combine_rows), _p(tile_expert), _p(expert_offsets),
+             _p(expert_counts), _p(mtiles), max_mtiles, _p(chunks), _p(counters), _p(stats),
+             _p(scratch), scratch.numel() * 4, _stream(flat))
+    else:
+        if route_count is not None and route_count.dtype != torch.int32:
+            raise TypeError("route_count must be a device int32 scalar tensor")
+        if capacity_dev is not None and capacity_dev.dtype != torch.int64:
+            raise TypeError("capacity_dev must be a device int64 scalar tensor")
+        call("b200moe_pack_routes_device_bounds", _p(flat), _p(route_weights), routes,
+             _p(route_count), num_experts, _p(local_index), int(expert_start),
+             num_local_experts, _p(expert_base), -1 if capacity is None else int(capacity),
+             _p(capacity_dev), row_capacity, _p(row_route), _p(route_row), _p(combine_rows),
+             _p(tile_expert), _p(expert_offsets), _p(expert_counts), _p(mtiles), max_mtiles,
+             _p(chunks), _p(counters), _p(stats), _p(scratch), scratch.numel() * 4,
+             _stream(flat))
     return PackedRoutes(routes, row_capacity, max_mtiles, row_route, route_row, combine_rows,
                         tile_expert, expert_offsets, expert_counts, mtiles, counters, chunks)
 
@@ -257,3 +273,77 @@ def ep_return_rows(expert_ids, owner, ep_size, num_experts, route_dest_slot, rou
          _p(route_dest_slot), _host_i32(route_offsets), int(num_rows_returned), _p(rows),
          _stream(flat))
     return rows
+
+
+# ---------------------------------------------------------------------------
+# Expert-parallel exchange over NVLink peer memory (see nvl.py for the buffers).
+# ---------------------------------------------------------------------------
+def nvl_buffers(layer, device: torch.device, group):
+    """The NVLink exchange buffer for this layer's shape on `group` (nvl.py)."""
+    from . import nvl
+    return nvl.buffers_for(layer, device, group)
+
+
+def nvl_histogram_send(expert_ids: torch.Tensor, num_tokens: int, top_k: int, rank: int,
+                       bufs) -> None:
+    """This rank's per-expert route counts and token count to every peer."""
+    call("b200moe_nvl_histogram_send", _p(expert_ids) if num_tokens else None, num_tokens,
+         top_k, bufs.num_experts, rank, bufs.ep_size, bufs.peer_bases, bufs.layout_ptr,
+         bufs.stream_ptr())
+
+
+def nvl_histogram_wait(top_k: int, rank: int, bufs, capacity_factor: float | None):
+    """-> (expert_base int32 [E], global_tokens int64 [1], capacity int64 [1]) on device."""
+    device = bufs.device
+    base = torch.empty(bufs.num_experts, device=device, dtype=torch.int32)
+    global_tokens = torch.empty(1, device=device, dtype=torch.int64)
+    capacity = torch.full((1,), -1, device=device, dtype=torch.int64)
+    call("b200moe_nvl_histogram_wait", top_k, bufs.num_experts, rank, bufs.ep_size,
+         bufs.peer_bases, bufs.layout_ptr, ctypes.c_double(float(capacity_factor or 0.0)),
+         _p(base), _p(global_tokens), _p(capacity), bufs.stream_ptr())
+    return base, global_tokens, capacity
+
+
+def nvl_dispatch(x: torch.Tensor, expert_ids: torch.Tensor, route_weights: torch.Tensor,
+                 owner: torch.Tensor, rank: int, bufs, send_token_slot, route_dest_slot, counts,
+                 bump_epoch: bool) -> torch.Tensor:
+    """Send this rank's tokens and route records; -> combine_rows int32 [T*k]."""
+    tokens, top_k = expert_ids.shape
+    combine_rows = torch.empty(tokens * top_k, device=bufs.device, dtype=torch.int32)
+    call("b200moe_nvl_dispatch", _p(x) if tokens else None, bufs.hidden,
+         _p(expert_ids) if tokens else None, _p(route_weights) if tokens else None, tokens,
+         top_k, bufs.num_experts, _p(owner), rank, bufs.ep_size,
+         _p(send_token_slot) if tokens else None, _p(route_dest_slot) if tokens else None,
+         _p(counts) if tokens else None, bufs.peer_bases, bufs.layout_ptr, bufs.max_tokens,
+         int(bool(bump_epoch)), _p(combine_rows) if tokens else None, bufs.stream_ptr())
+    return combine_rows
+
+
+def nvl_receive(rank: int, bufs):
+    """-> (ids int64, token_of_route int32, weights bf16, src_rank int32, src_route int32)
+    of length bufs.max_routes, and the received count (device int32 [1])."""
+    n = bufs.max_routes
+    device = bufs.device
+    ids = torch.empty(n, device=device, dtype=torch.int64)
+    token_of_route = torch.empty(n, device=device, dtype=torch.int32)
+    weights = torch.empty(n, device=device, dtype=torch.bfloat16)
+    src_rank = torch.empty(n, device=device, dtype=torch.int32)
+    src_route = torch.empty(n, device=device, dtype=torch.int32)
+    count = torch.empty(1, device=device, dtype=torch.int32)
+    call("b200moe_nvl_receive", rank, bufs.ep_size, bufs.peer_bases, bufs.layout_ptr,
+         bufs.max_tokens, _p(ids), _p(token_of_route), _p(weights), _p(src_rank),
+         _p(src_route), _p(count), bufs.stream_ptr())
+    return ids, token_of_route, weights, src_rank, src_route, count
+
+
+def nvl_return(y: torch.Tensor, src_rank: torch.Tensor, src_route: torch.Tensor,
+               count: torch.Tensor, rank: int, bufs) -> None:
+    """Rows of the received routes back to their sources' return buffers."""
+    call("b200moe_nvl_return", _p(y), bufs.hidden, _p(src_rank), _p(src_route), _p(count),
+         y.size(0), bufs.max_tokens * bufs.top_k, rank, bufs.ep_size, bufs.peer_bases,
+         bufs.layout_ptr, bufs.stream_ptr())
+
+
+def nvl_wait_return(rank: int, bufs) -> None:
+    call("b200moe_nvl_wait_return", rank, bufs.ep_size, bufs.peer_bases, bufs.layout_ptr,
+         bufs.stream_ptr())

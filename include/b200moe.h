@@ -89,9 +89,11 @@ B200MOE_API int b200moe_device_status(int *status, int clear);
  * Replaces ExpertParallelMoE._route softmax/topk/renorm/cast,
  * nanovllm/layers/moe.py:872-878 (the gate projection moe.py:871 stays a
  * library GEMM in the caller).
- * Ranking: descending logit, ties broken by the lower expert index.  Softmax
- * is monotone, so this is the reference's top-k of probabilities with a
- * defined tie order.
+ * The result equals, bit for bit, what the reference's torch calls return on
+ * a CUDA device: the same fp32 softmax arithmetic (per-lane then butterfly
+ * sum), the same top-k order for equal probabilities (torch's gather order
+ * followed by its 32-wide bitonic sort), and the same renormalisation sum
+ * order, so ids and bf16 weights match even when bf16 logits tie.
  *   logits     [num_tokens, num_experts] of logits_dtype (BF16/F16/F32), row-major
  *   weights    [num_tokens, top_k] bf16 out
  *   expert_ids [num_tokens, top_k] int64 out
@@ -154,6 +156,30 @@ B200MOE_API int b200moe_pack_routes(int64_t *expert_ids, void *route_weights, in
                         int64_t *stats, void *scratch, size_t scratch_bytes, void *stream);
 
 /*
+ * b200moe_pack_routes with device-side bounds, for callers whose route count
+ * or capacity exists only on the GPU (the expert-parallel receiver below,
+ * inside a CUDA graph).  Same arguments and results as b200moe_pack_routes
+ * plus:
+ *   route_count  device int32 or NULL: only routes [0, *route_count) are
+ *                packed (clamped to num_routes); the per-route outputs of
+ *                the others (route_row, combine_rows) are left unwritten and
+ *                their ids are never read.  num_routes still sizes the layout
+ *                (row_capacity, max_mtiles, scratch) and is the row_route
+ *                sentinel.
+ *   capacity_dev device int64 or NULL: overrides `capacity` (< 0: no limit).
+ * Same reference lines as b200moe_pack_routes (moe.py:879-919, :491-517,
+ * :783-868, :680-771).
+ */
+B200MOE_API int b200moe_pack_routes_device_bounds(
+    int64_t *expert_ids, void *route_weights, int64_t num_routes, const int32_t *route_count,
+    int num_experts, const int64_t *local_index, int expert_start, int num_local_experts,
+    const int32_t *expert_base, int64_t capacity, const int64_t *capacity_dev,
+    int64_t row_capacity, int32_t *row_route, int32_t *route_row, int32_t *combine_rows,
+    int32_t *tile_expert, int32_t *expert_offsets, int32_t *expert_counts, int32_t *mtiles,
+    int64_t max_mtiles, int32_t *chunks, int32_t *counters, int64_t *stats, void *scratch,
+    size_t scratch_bytes, void *stream);
+
+/*
  * b200moe_pack_routes for callers that cannot provide scratch memory.  No
  * counterpart in the reference: it exists for hosts that have committed
  * (nearly) all device memory to their own fixed pools, or that drive this
@@ -162,15 +188,21 @@ B200MOE_API int b200moe_pack_routes(int64_t *expert_ids, void *route_weights, in
  * library instead of a caller buffer.
  *  - Same arguments and results as b200moe_pack_routes, minus scratch and
  *    the row-chunk list (counters[B200MOE_CNT_CHUNKS] = 0).
- *  - Limit: b200moe_pack_static_scratch_capacity() bytes (256 KiB), i.e.
- *    b200moe_pack_scratch_bytes(num_routes, num_experts) must not exceed it;
- *    every call with up to 65,536 routes and up to 1,023 experts fits, and
- *    at 128 experts any route count up to 520,192 does.  Larger calls fail
- *    with B200MOE_EINVAL and a message.  Each GPU that loads the library
- *    holds the array until the process exits.
+ *  - Limit: a call is accepted exactly when
+ *    b200moe_pack_scratch_bytes(num_routes, num_experts) <=
+ *    b200moe_pack_static_scratch_capacity() (256 KiB); check that before
+ *    calling.  Other calls fail with B200MOE_EINVAL and a message.  The
+ *    need is not monotone in num_routes (the packing kernels widen their
+ *    route chunks once more than 512 blocks would be needed): at 128
+ *    experts, 520,193 to 524,288 routes are rejected while 600,000 fit.
+ *    Every call with up to 65,536 routes and up to 1,023 experts fits.
+ *    Each GPU that loads the library holds the array until the process
+ *    exits.
  *  - Allocates nothing: no cudaMalloc/cudaFree.  The first call on each
- *    device looks up the array's device address (cudaGetSymbolAddress) with
- *    that device current; make that first call before any stream capture.
+ *    device (and the first call after that device's context was re-created,
+ *    e.g. after cudaDeviceReset) looks up the array's device address
+ *    (cudaGetSymbolAddress) with that device current; make that call before
+ *    any stream capture.
  *  - All calls on a device share the one array and every call overwrites the
  *    part it uses (nothing needs to start at zero); calls whose kernels
  *    overlap on the GPU (different streams without ordering) race and must be
@@ -337,6 +369,102 @@ B200MOE_API int b200moe_ep_return_rows(const int64_t *expert_ids, const int32_t 
                            int num_experts, int ep_size, const int32_t *route_dest_slot,
                            const int32_t *route_offsets_host, int64_t num_rows_returned,
                            int32_t *combine_rows, void *stream);
+
+/* ---- expert-parallel exchange over NVLink peer memory ---------------------
+ * Graph-safe replacement of the reference's cross-DP exchange (all-gather of
+ * every replica's tokens, global routing on every rank, reduction of
+ * [N*T, H] partial outputs: nanovllm/layers/moe.py:942-1018, and the
+ * rank-0 all-to-all experiment :1020-1216).  Each EP rank owns one exchange
+ * buffer (b200moe_nvl_buffer_bytes) and maps every peer's buffer into its
+ * address space (b200moe_ipc_handle / b200moe_ipc_open); `peer_bases` is a
+ * HOST array of ep_size device pointers (256-byte aligned), entry r being
+ * rank r's buffer as mapped in the calling process (own buffer included).
+ * All sizes that vary per step stay on the device, so every call can be
+ * captured in a CUDA graph.  One exchange is:
+ *   [capacity] b200moe_nvl_histogram_send, _wait -> expert_base, capacity
+ *   b200moe_pack_routes(_device_bounds) over own routes with capacity
+ *   b200moe_ep_plan                    -> slots and counts
+ *   b200moe_nvl_dispatch               (bump_epoch = 1 unless the histogram ran)
+ *   b200moe_nvl_receive                -> received routes (device count)
+ *   local packing / expert GEMMs over the received routes
+ *   b200moe_nvl_return                 -> rows into the sources' return buffers
+ *   b200moe_nvl_wait_return            -> then b200moe_combine over the
+ *                                         return buffer with combine_rows
+ * Every rank must make the same sequence of calls (an exchange is a
+ * collective).  Waits on peers are bounded (2 s); on expiry the device
+ * status word gets bit 0 and the kernels return.  ep_size <= 16.
+ */
+#define B200MOE_NVL_LAYOUT_WORDS 10
+
+/* Bytes of one rank's exchange buffer for batches of up to max_tokens
+ * tokens per rank (or -1 on bad arguments); fills layout[10] (byte offsets
+ * of its sections, used by the calls below). */
+B200MOE_API int64_t b200moe_nvl_buffer_bytes(int ep_size, int64_t max_tokens, int top_k,
+                                             int num_experts, int num_local_experts, int hidden,
+                                             int64_t *layout);
+
+/* CUDA IPC of device memory: a 64-byte handle of the allocation holding
+ * `ptr` and ptr's offset inside it; open maps a peer's allocation (peer
+ * access enabled lazily) and returns the peer's pointer; close unmaps. */
+B200MOE_API int b200moe_ipc_handle(const void *ptr, void *handle, int64_t *offset);
+B200MOE_API int b200moe_ipc_open(const void *handle, int64_t offset, void **ptr);
+B200MOE_API int b200moe_ipc_close(void *ptr, int64_t offset);
+
+/* Capacity agreement, in two halves so that one device can drive several
+ * ranks in turn.  Send: this rank's per-expert route counts and token count
+ * go to every peer (advances the exchange epoch).  Wait: once every peer's
+ * counts are in, (device) expert_base[e] = routes to e of lower ranks,
+ * *global_tokens = tokens of all ranks, and (capacity_factor > 0)
+ * *capacity = max(1, ceil(factor * global_tokens * top_k / num_experts)),
+ * the reference's formula (moe.py:882-885). */
+B200MOE_API int b200moe_nvl_histogram_send(const int64_t *expert_ids, int64_t num_tokens,
+                                           int top_k, int num_experts, int rank, int ep_size,
+                                           const uint64_t *peer_bases, const int64_t *layout,
+                                           void *stream);
+B200MOE_API int b200moe_nvl_histogram_wait(int top_k, int num_experts, int rank, int ep_size,
+                                           const uint64_t *peer_bases, const int64_t *layout,
+                                           double capacity_factor, int32_t *expert_base,
+                                           int64_t *global_tokens, int64_t *capacity,
+                                           void *stream);
+
+/* Dispatch (after capacity and b200moe_ep_plan): each token row once per
+ * destination owning one of its kept routes, the route records
+ * {expert, token slot, bf16 weight bits, route id} and the counts, written
+ * into the destinations' regions for this rank.  combine_rows[r] (device,
+ * [num_tokens * top_k]) = r for routes sent anywhere, else
+ * num_tokens * top_k. */
+B200MOE_API int b200moe_nvl_dispatch(const void *x, int hidden, const int64_t *expert_ids,
+                                     const void *route_weights, int64_t num_tokens, int top_k,
+                                     int num_experts, const int32_t *owner, int rank,
+                                     int ep_size, const int32_t *send_token_slot,
+                                     const int32_t *route_dest_slot, const int32_t *counts,
+                                     const uint64_t *peer_bases, const int64_t *layout,
+                                     int64_t max_tokens, int bump_epoch, int32_t *combine_rows,
+                                     void *stream);
+
+/* Receiver: waits for every source, then flat arrays of the received routes
+ * in (source, slot) order, [ep_size * route_cap] each (route_cap = layout[8]):
+ * global expert ids, token_of_route (row of the exchange buffer's token
+ * section viewed as [ep_size * max_tokens, hidden]), bf16 weights, source
+ * rank, source route id; *route_count (device) = number received. */
+B200MOE_API int b200moe_nvl_receive(int rank, int ep_size, const uint64_t *peer_bases,
+                                    const int64_t *layout, int64_t max_tokens,
+                                    int64_t *expert_ids, int32_t *token_of_route,
+                                    void *route_weights, int32_t *src_rank, int32_t *src_route,
+                                    int32_t *route_count, void *stream);
+
+/* Return: y [max_routes, hidden] bf16 (received-route order); rows
+ * j < *route_count go to rank src_rank[j]'s return buffer at row
+ * src_route[j] (< max_source_routes). */
+B200MOE_API int b200moe_nvl_return(const void *y, int hidden, const int32_t *src_rank,
+                                   const int32_t *src_route, const int32_t *route_count,
+                                   int64_t max_routes, int64_t max_source_routes, int rank,
+                                   int ep_size, const uint64_t *peer_bases, const int64_t *layout,
+                                   void *stream);
+
+/* Source: waits until every destination returned its rows. */
+B200MOE_API int b200moe_nvl_wait_return(int rank, int ep_size, const uint64_t *peer_bases,
+                                        const int64_t *layout, void *stream);
 
 #ifdef __cplusplus
 }

@@ -55,8 +55,14 @@ class CpuOps:
 
     def pack_routes(self, expert_ids, route_weights, num_experts, num_local_experts, *,
                     local_index=None, expert_start=0, expert_base=None, capacity=None,
-                    stats=None):
+                    stats=None, route_count=None, capacity_dev=None):
         flat = expert_ids.view(-1)
+        if route_count is not None:
+            flat = flat[:int(route_count.reshape(-1)[0])]
+            route_weights = None if route_weights is None else route_weights.view(-1)[:flat.numel()]
+        if capacity_dev is not None:
+            capacity = int(capacity_dev.reshape(-1)[0])
+            capacity = None if capacity < 0 else capacity
         dropped = 0
         if capacity is not None:
             w = (route_weights.float().numpy() if route_weights is not None
@@ -202,3 +208,126 @@ class CpuOps:
         off = np.asarray(list(route_offsets) + [0])
         rows = np.where((dest >= 0) & (rs >= 0), off[np.maximum(dest, 0)] + rs, num_rows_returned)
         return torch.from_numpy(rows.astype(np.int32))
+
+    # ---- expert-parallel exchange over peer memory (stand-in transport) ----
+    # The NVLink exchange's phases with the same tensor contracts; the rows
+    # and records travel through gloo object collectives on the MoE group
+    # instead of peer stores, so the layer's host logic runs on CPU ranks.
+    def nvl_buffers(self, layer, device, group):
+        bufs = getattr(layer, "_cpu_exchange", None)
+        if bufs is None:
+            bufs = CpuExchange(layer, group)
+            layer._cpu_exchange = bufs
+        return bufs
+
+    def nvl_histogram_send(self, expert_ids, num_tokens, top_k, rank, bufs):
+        import torch.distributed as dist
+        flat = expert_ids.reshape(-1).numpy()
+        flat = flat[(flat >= 0) & (flat < bufs.num_experts)]
+        mine = np.append(np.bincount(flat, minlength=bufs.num_experts), num_tokens)
+        everyone = [None] * bufs.ep_size
+        dist.all_gather_object(everyone, mine.astype(np.int64), group=bufs.group)
+        bufs.hist = np.stack(everyone)
+
+    def nvl_histogram_wait(self, top_k, rank, bufs, capacity_factor):
+        import math
+        E = bufs.num_experts
+        base = torch.from_numpy(bufs.hist[:rank, :E].sum(axis=0).astype(np.int32))
+        tokens = int(bufs.hist[:, E].sum())
+        cap = (max(1, math.ceil(capacity_factor * tokens * top_k / E))
+               if capacity_factor else -1)
+        return base, torch.tensor([tokens]), torch.tensor([cap])
+
+    def nvl_dispatch(self, x, expert_ids, route_weights, owner, rank, bufs, send_token_slot,
+                     route_dest_slot, counts, bump_epoch):
+        import torch.distributed as dist
+        T, k = expert_ids.shape
+        n = bufs.ep_size
+        dest = self._dest(expert_ids.numpy(), owner.numpy(), n, bufs.num_experts)
+        payload = {d: ([], []) for d in range(n)}
+        combine_rows = np.full(T * k, T * k, dtype=np.int32)
+        if T:
+            tok_slot = send_token_slot.numpy()
+            rs = route_dest_slot.numpy()
+            bits = route_weights.reshape(-1).view(torch.int16).numpy().astype(np.int32) & 0xFFFF
+            ids = expert_ids.reshape(-1).numpy()
+            xs = x.view(torch.int16).numpy()
+            for t in range(T):
+                for d in range(n):
+                    if tok_slot[t, d] >= 0:
+                        payload[d][0].append((int(tok_slot[t, d]), xs[t].copy()))
+            for r in range(T * k):
+                d = dest[r]
+                if d >= 0 and rs[r] >= 0:
+                    payload[d][1].append((int(rs[r]), int(ids[r]), int(tok_slot[r // k, d]),
+                                          int(bits[r]), r))
+                    combine_rows[r] = r
+        everyone = [None] * n
+        dist.all_gather_object(everyone, payload, group=bufs.group)
+        bufs.received = []
+        for s in range(n):
+            rows, records = everyone[s][rank]
+            for slot, row in rows:
+                bufs.tokens.view(torch.int16)[s * bufs.max_tokens + slot] = torch.from_numpy(row)
+            bufs.received.append(sorted(records))
+        return torch.from_numpy(combine_rows)
+
+    def nvl_receive(self, rank, bufs):
+        m = bufs.max_routes
+        ids = torch.full((m,), -1, dtype=torch.int64)
+        tor = torch.zeros(m, dtype=torch.int32)
+        w = torch.zeros(m, dtype=torch.int16)
+        src_rank = torch.zeros(m, dtype=torch.int32)
+        src_route = torch.zeros(m, dtype=torch.int32)
+        j = 0
+        for s, records in enumerate(bufs.received):
+            for _, expert, slot, bits, route in records:
+                ids[j], tor[j] = expert, s * bufs.max_tokens + slot
+                w[j] = np.int16(np.uint16(bits).view(np.int16))
+                src_rank[j], src_route[j] = s, route
+                j += 1
+        return ids, tor, w.view(torch.bfloat16), src_rank, src_route, torch.tensor([j],
+                                                                                  dtype=torch.int32)
+
+    def nvl_return(self, y, src_rank, src_route, count, rank, bufs):
+        import torch.distributed as dist
+        n = int(count.reshape(-1)[0])
+        out = {s: [] for s in range(bufs.ep_size)}
+        ys = y.view(torch.int16).numpy()
+        for j in range(n):
+            out[int(src_rank[j])].append((int(src_route[j]), ys[j].copy()))
+        everyone = [None] * bufs.ep_size
+        dist.all_gather_object(everyone, out, group=bufs.group)
+        for d in range(bufs.ep_size):
+            for route, row in everyone[d][rank]:
+                bufs.returned.view(torch.int16)[route] = torch.from_numpy(row)
+
+    def nvl_wait_return(self, rank, bufs):
+        return None
+
+
+class CpuExchange:
+    """CPU stand-in of one rank's NVLink exchange buffer (token rows received
+    per source, route rows returned to this rank) and its geometry."""
+
+    def __init__(self, layer, group) -> None:
+        self.group = group
+        self.ep_size = layer.ep_size
+        self.max_tokens = int(getattr(layer, "nvl_max_tokens", None) or 8192)
+        self.top_k = layer.top_k
+        self.num_experts = layer.num_experts
+        self.hidden = layer.hidden_size
+        self.route_cap = self.max_tokens * min(layer.top_k, layer.num_local_experts)
+        self.max_routes = self.ep_size * self.route_cap
+        self.tokens = torch.zeros((self.ep_size * self.max_tokens, self.hidden),
+                                  dtype=torch.bfloat16)
+        self.returned = torch.zeros((self.max_tokens * self.top_k, self.hidden),
+                                    dtype=torch.bfloat16)
+        self.received = []
+        self.hist = None
+
+    def tokens_view(self):
+        return self.tokens
+
+    def returned_view(self, rows):
+        return self.returned[:rows]

@@ -12,8 +12,9 @@ functions against golden vectors produced by the reference itself
 its outputs).
 
 Conventions shared with the CUDA library:
-  * top-k ranks by descending logit, ties to the lower expert index (softmax
-    is monotone; the reference's torch.topk leaves tie order unspecified);
+  * the router reproduces torch's CUDA softmax, top-k (including the order
+    of equal probabilities) and renormalisation sum, the reference's GPU
+    path (moe.py:872-878);
   * rounding points of the reference's GPU path (moe.py:742-746, :848-858):
     gate/up stored in bf16, silu and the product rounded to bf16, the route
     weight applied to the fp32 down accumulator before the bf16 store, the
@@ -53,13 +54,120 @@ def from_bf16_bits(bits) -> np.ndarray:
 
 
 # ---------------------------------------------------------------------------
-# Router (moe.py:870-878)
+# Router (moe.py:870-878): the arithmetic and selection order of
+#   F.softmax(logits, -1, dtype=float32); torch.topk(probs, k);
+#   w /= w.sum(-1, keepdim=True); w.to(bf16)
+# as torch 2.x computes them on a CUDA device (the reference's GPU path).
 # ---------------------------------------------------------------------------
 def softmax_f32(logits: np.ndarray) -> np.ndarray:
+    """torch's persistent warp softmax for rows of <= 1024 fp32 values:
+    with P = next power of two >= E and L = min(P, 32) lanes, lane l holds
+    elements l + L*i; p = exp(v - max); each lane sums its elements in i
+    order, a butterfly (xor L/2 ... 1) sums the lanes; out = p / sum.
+    numpy's float32 exp stands in for CUDA's expf (they agree to within an
+    ulp; the tie-order tests feed probabilities recorded on a GPU instead)."""
     logits = np.asarray(logits, dtype=np.float32)
+    rows, experts = logits.shape
     m = logits.max(axis=-1, keepdims=True)
     e = np.exp(logits - m, dtype=np.float32)
-    return (e / e.sum(axis=-1, keepdims=True, dtype=np.float32)).astype(np.float32)
+    width = 1
+    while width < experts:
+        width *= 2
+    lanes = min(width, 32)
+    padded = np.zeros((rows, width), dtype=np.float32)
+    padded[:, :experts] = e
+    lane_sum = np.zeros((rows, lanes), dtype=np.float32)
+    for i in range(width // lanes):
+        lane_sum = (lane_sum + padded[:, i * lanes:(i + 1) * lanes]).astype(np.float32)
+    off = lanes // 2
+    idx = np.arange(lanes)
+    while off:
+        lane_sum = (lane_sum + lane_sum[:, idx ^ off]).astype(np.float32)
+        off //= 2
+    return (e / lane_sum[:, :1]).astype(np.float32)
+
+
+def _bitonic_exchange(key, ids, lo, hi, direction):
+    """One compare-exchange of torch's bitonic sort (descending comparator
+    a > b): exchange when ((key[lo] > key[hi] and lo valid) or hi invalid)
+    equals the direction.  ids < 0 mark invalid padding."""
+    ka, kb = key[:, lo], key[:, hi]
+    va, vb = ids[:, lo] >= 0, ids[:, hi] >= 0
+    swap = ((ka > kb) & va) | ~vb
+    ex = swap == direction
+    key[ex, lo], key[ex, hi] = kb[ex], ka[ex]
+    ia, ib = ids[:, lo].copy(), ids[:, hi].copy()
+    ids[ex, lo], ids[ex, hi] = ib[ex], ia[ex]
+
+
+def topk_from_probs(probs: np.ndarray, top_k: int) -> tuple[np.ndarray, np.ndarray]:
+    """torch.topk(probs, k) (largest, sorted) on a CUDA device, k <= 32.
+
+    The selection kernel writes the elements above the k-th largest value in
+    ascending index order, then the first elements equal to it (ascending
+    index); the k pairs are then sorted by a 32-wide bitonic network whose
+    exchange is not stable, which fixes the order of equal values."""
+    probs = np.asarray(probs, dtype=np.float32)
+    rows, experts = probs.shape
+    if not 1 <= top_k <= min(32, experts):
+        raise ValueError("top_k must be in [1, min(32, num_experts)]")
+    order = np.lexsort((np.broadcast_to(np.arange(experts), probs.shape), -probs))[:, :top_k]
+    kth = np.take_along_axis(probs, order[:, -1:], axis=1)
+    gathered = np.empty((rows, top_k), dtype=np.int64)
+    for r in range(rows):
+        above = np.sort(order[r][probs[r, order[r]] > kth[r, 0]])
+        equal = np.nonzero(probs[r] == kth[r, 0])[0][: top_k - above.size]
+        gathered[r] = np.concatenate([above, equal])
+    key = np.zeros((rows, 32), dtype=np.float32)
+    ids = np.full((rows, 32), -1, dtype=np.int64)
+    key[:, :top_k] = np.take_along_axis(probs, gathered, axis=1)
+    ids[:, :top_k] = gathered
+    if top_k > 1:
+        pos = np.arange(32)
+        size = 2
+        while size < 32:
+            stride = size // 2
+            while stride:
+                lo = pos[(pos & stride) == 0]
+                for a in lo:
+                    _bitonic_exchange(key, ids, a, a + stride, bool(a & size))
+                stride //= 2
+            size *= 2
+        stride = 16
+        while stride:
+            for a in pos[(pos & stride) == 0]:
+                _bitonic_exchange(key, ids, a, a + stride, False)
+            stride //= 2
+    return key[:, :top_k].copy(), ids[:, :top_k].copy()
+
+
+def renorm_sum(w: np.ndarray) -> np.ndarray:
+    """torch's sum over the last dim of a [T, k] fp32 tensor on CUDA: thread
+    t < W (W = largest power of two <= k) adds slots t and t + W, then a
+    shuffle-down tree with offsets W/2 ... 1."""
+    w = np.asarray(w, dtype=np.float32)
+    k = w.shape[1]
+    width = 1
+    while width * 2 <= k:
+        width *= 2
+    acc = w[:, :width].copy()
+    for t in range(width):
+        if t + width < k:
+            acc[:, t] = (acc[:, t] + w[:, t + width]).astype(np.float32)
+    off = width // 2
+    while off:
+        acc[:, :off] = (acc[:, :off] + acc[:, off:2 * off]).astype(np.float32)
+        off //= 2
+    return acc[:, 0]
+
+
+def route_from_probs(probs: np.ndarray, top_k: int, renormalize: bool
+                     ) -> tuple[np.ndarray, np.ndarray]:
+    """top-k + optional renorm + bf16 cast of given fp32 probabilities."""
+    w, ids = topk_from_probs(probs, top_k)
+    if renormalize:
+        w = (w / renorm_sum(w)[:, None]).astype(np.float32)
+    return bf16_round(w), ids
 
 
 def route_topk(logits: np.ndarray, top_k: int, renormalize: bool
@@ -68,18 +176,7 @@ def route_topk(logits: np.ndarray, top_k: int, renormalize: bool
 
     Returns (weights as bf16-rounded float32 [T, k], ids int64 [T, k]).
     """
-    logits = np.asarray(logits, dtype=np.float32)
-    probs = softmax_f32(logits)
-    # Stable argsort of -logit: descending value, ascending index on ties.
-    order = np.argsort(-logits, axis=-1, kind="stable")[:, :top_k]
-    ids = order.astype(np.int64)
-    w = np.take_along_axis(probs, order, axis=-1).astype(np.float32)
-    if renormalize:
-        total = np.zeros(w.shape[0], dtype=np.float32)
-        for s in range(top_k):  # sequential fp32 sum over the slots
-            total = (total + w[:, s]).astype(np.float32)
-        w = (w / total[:, None]).astype(np.float32)
-    return bf16_round(w), ids
+    return route_from_probs(softmax_f32(logits), top_k, renormalize)
 
 
 def tie_tokens(logits: np.ndarray, top_k: int) -> np.ndarray:
@@ -226,6 +323,10 @@ def pack(flat_ids: np.ndarray, num_experts: int, num_local: int, expert_start: i
 # Expert math (Triton path numerics, moe.py:63-139, :742-770, :848-863)
 # ---------------------------------------------------------------------------
 def _t32(a) -> torch.Tensor:
+    """fp32 CPU tensor of a numpy array or a torch tensor (any device, bf16
+    allowed), so that large bf16 weights are widened one expert at a time."""
+    if isinstance(a, torch.Tensor):
+        return a.detach().to(device="cpu", dtype=torch.float32)
     return torch.as_tensor(np.asarray(a, dtype=np.float32))
 
 
@@ -234,7 +335,8 @@ def expert_rows(x: np.ndarray, w13: np.ndarray, w2: np.ndarray, flat_ids: np.nda
                 num_local: int, expert_start: int = 0,
                 local_index: np.ndarray | None = None) -> tuple[np.ndarray, np.ndarray]:
     """Per-route expert output y [R, H] (bf16-valued float32) and a mask of the
-    routes computed here.  x, w13, w2, flat_weights hold bf16 values."""
+    routes computed here.  x, w13, w2, flat_weights hold bf16 values; w13 and
+    w2 may be numpy arrays or (bf16) torch tensors."""
     flat = np.asarray(flat_ids, dtype=np.int64).reshape(-1)
     local = local_ids(flat, num_experts, num_local, expert_start, local_index)
     H = x.shape[1]
@@ -271,11 +373,19 @@ def combine(y: np.ndarray, route_rows: np.ndarray, num_tokens: int, top_k: int,
 def moe_forward(x: np.ndarray, logits: np.ndarray, w13: np.ndarray, w2: np.ndarray,
                 top_k: int, renormalize: bool, *, capacity: int | None = None,
                 num_local: int | None = None, expert_start: int = 0,
-                local_index: np.ndarray | None = None) -> dict:
-    """Full layer on one rank: route, capacity, local experts, combine."""
+                local_index: np.ndarray | None = None, probs: np.ndarray | None = None
+                ) -> dict:
+    """Full layer on one rank: route, capacity, local experts, combine.
+
+    ``probs`` (optional) are softmax probabilities computed elsewhere (a GPU
+    test passes torch's CUDA softmax so that exp rounding cannot differ);
+    selection, renormalisation and everything after run here."""
     num_tokens, num_experts = logits.shape
     num_local = w13.shape[0] if num_local is None else num_local
-    weights, ids = route_topk(logits, top_k, renormalize)
+    if probs is None:
+        weights, ids = route_topk(logits, top_k, renormalize)
+    else:
+        weights, ids = route_from_probs(probs, top_k, renormalize)
     weights, ids, keep = apply_capacity(weights, ids, num_experts, capacity)
     flat = ids.reshape(-1)
     tokens = np.arange(flat.size) // top_k

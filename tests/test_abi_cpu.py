@@ -56,3 +56,19 @@ def test_argument_errors_without_device():
                   16, null, 1, null, null, null, null)
     with pytest.raises(ValueError, match="ep_size"):
         _lib.call("b200moe_ep_plan", null, 1, 1, 8, null, 17, null, null, null, null)
+
+
+def test_static_scratch_limit_is_the_scratch_rule_not_a_route_bound():
+    """The no-scratch packing call accepts exactly the calls whose scratch need
+    fits the library's array; the need is not monotone in the route count
+    (route chunks widen once more than 512 blocks would be needed)."""
+    cap = int(_lib.LIB.b200moe_pack_static_scratch_capacity())
+    need = lambda r, e: int(_lib.LIB.b200moe_pack_scratch_bytes(r, e))  # noqa: E731
+    assert need(520_192, 128) <= cap < need(520_193, 128)
+    assert need(524_288, 128) > cap and need(600_000, 128) <= cap
+    null = ctypes.c_void_p(0)
+    for routes in (520_193, 524_288):
+        with pytest.raises(ValueError, match="static scratch"):
+            _lib.call("b200moe_pack_routes_static_scratch", null, null, routes, 128, null, 0,
+                      128, null, -1, 0, null, null, null, null, null, null, null, 0, null, null,
+                      null)

@@ -39,6 +39,14 @@ def make_layer(shape, seed, **kw):
     return layer, w13, w2, gate
 
 
+def gpu_logits(layer, x):
+    """The layer's own router logits (bf16 gate GEMM on the GPU) and torch's
+    CUDA softmax of them, for the oracle's routing."""
+    logits = layer.gate(x.to(DEV))
+    probs = torch.softmax(logits, dim=-1, dtype=torch.float32)
+    return logits.float().cpu().numpy(), probs.cpu().numpy()
+
+
 @pytest.fixture(autouse=True)
 def clean_status():
     _lib.device_status(clear=True)
@@ -86,9 +94,9 @@ def test_layer_matches_oracle_config1_shape_and_counters():
     layer, w13, w2, gate = make_layer(A, 31)
     x = wl.hidden_states(64, A.hidden, seed=33)
     out = layer(x.to(DEV))
-    logits = torch.nn.functional.linear(x, gate).float().numpy()
+    logits, probs = gpu_logits(layer, x)
     ref = mo.moe_forward(x.float().numpy(), logits, w13.float().numpy(), w2.float().numpy(), 8,
-                         True)
+                         True, probs=probs)
     close(out, ref["output"])
     assert layer.dispatch_assignment_count == 64 * 8
     assert layer.total_assignment_count == 64 * 8
@@ -99,10 +107,10 @@ def test_capacity_counters_match_oracle():
     layer, w13, w2, gate = make_layer(A, 41, expert_capacity_factor=0.5)
     x = wl.hidden_states(256, A.hidden, seed=43)
     out = layer(x.to(DEV))
-    logits = torch.nn.functional.linear(x, gate).float().numpy()
+    logits, probs = gpu_logits(layer, x)
     cap = mo.capacity_of(256, 8, 128, None, 0.5)
     ref = mo.moe_forward(x.float().numpy(), logits, w13.float().numpy(), w2.float().numpy(), 8,
-                         True, capacity=cap)
+                         True, capacity=cap, probs=probs)
     close(out, ref["output"])
     kept = int(ref["keep"].sum())
     assert layer.dispatch_assignment_count == kept

@@ -1,11 +1,12 @@
 """Expert parallelism on two GPUs over NCCL with the native kernels.
 
 Rank r holds experts [64r, 64r+64) of a 128-expert 30B-A3B-shaped layer and
-its own tokens.  With the all-to-all backend every route is computed by the
-same kernel arithmetic as on one GPU and combined in slot order at its
+its own tokens.  With the NVLink exchange backend every route is computed by
+the same kernel arithmetic as on one GPU and combined in slot order at its
 source, so the sharded output must equal the single-GPU layer bit for bit
-(both sides forced onto the tcgen05 engine); the all-gather backend sums
-bf16 partials in the collective and is compared with the usual tolerance.
+(both sides forced onto the tcgen05 engine), eagerly and replayed from a
+CUDA graph with new tokens; the all-gather backend sums bf16 partials in the
+collective and is compared with the usual tolerance.
 Skipped unless two GPUs are visible.
 """
 
@@ -46,9 +47,9 @@ def _build(rank, world, backend, kw, device):
     return layer
 
 
-def _tokens(rank, device):
+def _tokens(rank, device, step=0):
     import extend_nano_vllm_b200.workloads as wl
-    return wl.hidden_states(COUNTS[rank], 2048, seed=50 + rank, device=device)
+    return wl.hidden_states(COUNTS[rank], 2048, seed=50 + rank + 10 * step, device=device)
 
 
 def _worker(rank, port, backend, kw, queue):
@@ -66,14 +67,28 @@ def _worker(rank, port, backend, kw, queue):
         with torch.no_grad():
             out = layer(_tokens(rank, device))
         torch.cuda.synchronize()
+        replays = []
+        if backend == "all_to_all_nvlink":
+            # The exchange captured in a CUDA graph, replayed with new tokens.
+            x = _tokens(rank, device).clone()
+            graph = torch.cuda.CUDAGraph()
+            with torch.no_grad():
+                with torch.cuda.graph(graph):
+                    static_out = layer(x)
+                for step in range(2):
+                    x.copy_(_tokens(rank, device, step + 1))
+                    graph.replay()
+                    torch.cuda.synchronize()
+                    replays.append(static_out.float().cpu().numpy())
+            del graph
         from extend_nano_vllm_b200 import device_status
         queue.put((rank, out.float().cpu().numpy(), layer.dispatch_assignment_count,
-                   layer.dropped_assignment_count, device_status()))
+                   layer.dropped_assignment_count, device_status(), replays))
         dist.barrier()
         dist.destroy_process_group()
     except Exception:  # noqa: BLE001 - reported to the parent
         import traceback
-        queue.put((rank, "error", traceback.format_exc(), None, None))
+        queue.put((rank, "error", traceback.format_exc(), None, None, None))
 
 
 @pytest.mark.timeout(600)
@@ -107,10 +122,16 @@ def test_two_gpu_expert_parallel_matches_one_gpu(backend, kw):
     with torch.no_grad():
         expected = full(torch.cat([_tokens(0, device), _tokens(1, device)])).float().cpu().numpy()
     got = np.concatenate([results[0][1], results[1][1]])
+    assert results[0][2] + results[1][2] == full.dispatch_assignment_count
     if backend == "all_to_all_nvlink":
         np.testing.assert_array_equal(got, expected)
         assert results[0][3] + results[1][3] == full.dropped_assignment_count
+        for step in range(2):
+            with torch.no_grad():
+                want = full(torch.cat([_tokens(0, device, step + 1),
+                                       _tokens(1, device, step + 1)])).float().cpu().numpy()
+            np.testing.assert_array_equal(
+                np.concatenate([results[0][5][step], results[1][5][step]]), want)
     else:
         scale = float(np.abs(expected).max())
         assert np.abs(got - expected).max() <= 1e-2 * scale
-    assert results[0][2] + results[1][2] == full.dispatch_assignment_count

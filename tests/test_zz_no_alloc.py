@@ -26,7 +26,8 @@ def _p(t):
     return None if t is None else ctypes.c_void_p(t.data_ptr())
 
 
-def _pack_static(ids, weights, num_experts, num_local, capacity):
+def _pack_static(ids, weights, num_experts, num_local, capacity, local_index=None,
+                 expert_start=0):
     """Same outputs as ops.pack_routes, through the no-scratch entry point."""
     flat = ids.view(-1)
     routes = flat.numel()
@@ -44,7 +45,8 @@ def _pack_static(ids, weights, num_experts, num_local, capacity):
         counters=torch.empty(_lib.NUM_COUNTERS, **i32))
     stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
     _lib.call("b200moe_pack_routes_static_scratch", _p(flat), _p(weights.view(-1)), routes,
-              num_experts, None, 0, num_local, None, -1 if capacity is None else capacity,
+              num_experts, _p(local_index), expert_start, num_local, None,
+              -1 if capacity is None else capacity,
               row_capacity, _p(out["row_route"]), _p(out["route_row"]), _p(out["combine_rows"]),
               _p(out["tile_expert"]), _p(out["expert_offsets"]), _p(out["expert_counts"]),
               _p(out["mtiles"]), max_mtiles, _p(out["counters"]), None, stream)
@@ -75,6 +77,43 @@ def test_static_scratch_pack_matches_caller_scratch_pack_twice(tokens, capacity)
                 tensor, expect = tensor[:_lib.CNT_CHUNKS], expect[:_lib.CNT_CHUNKS]
             np.testing.assert_array_equal(tensor.cpu().numpy(), expect.cpu().numpy(),
                                           err_msg=f"{name} (call {call})")
+    assert _lib.device_status(clear=True) == 0
+
+
+def _compare(ref, got, tag):
+    for name, tensor in got.items():
+        expect = getattr(ref, name)
+        if name == "mtiles":
+            n = int(ref.counters[_lib.CNT_MTILES])
+            tensor, expect = tensor[:n], expect[:n]
+        if name == "counters":
+            assert int(tensor[_lib.CNT_CHUNKS]) == 0
+            tensor, expect = tensor[:_lib.CNT_CHUNKS], expect[:_lib.CNT_CHUNKS]
+        np.testing.assert_array_equal(tensor.cpu().numpy(), expect.cpu().numpy(),
+                                      err_msg=f"{name} ({tag})")
+
+
+@pytest.mark.parametrize("placement", ["shard", "round_robin"])
+def test_static_scratch_pack_expert_parallel_placements(placement):
+    """An EP rank's view: 32 of 128 experts local, either the contiguous
+    shard starting at expert 64 or every fourth expert through local_index."""
+    dev = torch.device("cuda")
+    local_index = None
+    expert_start = 0
+    if placement == "shard":
+        expert_start = 64
+    else:
+        local_index = torch.tensor([(e // 4 if e % 4 == 1 else -1) for e in range(128)],
+                                   dtype=torch.int64, device=dev)
+    for call in range(2):
+        logits = wl.uniform_logits(2048, 128, seed=90 + call).to(dev)
+        weights, ids = ops.route_topk(logits, 8, True)
+        ref = ops.pack_routes(ids.clone().view(-1), weights.clone().view(-1), 128, 32,
+                              local_index=local_index, expert_start=expert_start)
+        got = _pack_static(ids.clone(), weights.clone(), 128, 32, None, local_index,
+                           expert_start)
+        torch.cuda.synchronize()
+        _compare(ref, got, f"{placement}, call {call}")
     assert _lib.device_status(clear=True) == 0
 
 
