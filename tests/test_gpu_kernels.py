@@ -5,9 +5,12 @@ for bit.  Floating point tolerances:
   * router ids and weights: bit-exact against the oracle's selection over
     torch's CUDA softmax (the reference's GPU routing); <= 1 bf16 ulp
     against the oracle's own numpy softmax;
-  * expert rows / layer outputs: max |diff| <= 1e-2 * max|ref| and
-    mean |diff| <= 1e-3 * max|ref| (fp32 accumulation order differs; the
-    rounding points are the same);
+  * expert rows / layer outputs: max |diff| <= 2^-7 * max|ref| and
+    mean |diff| <= 2e-4 * max|ref| against the oracle (fp32 accumulation
+    order differs; the rounding points are the same).  The reference's own
+    Triton path, whose outputs these kernels equal bit for bit
+    (test_gpu_reference_triton.py), sits at up to 0.0056 * max|ref| from the
+    oracle on the 235B shape;
   * combine: bit-exact (same fp32 slot-order sum).
 """
 
@@ -30,7 +33,7 @@ def bits(t: torch.Tensor) -> np.ndarray:
     return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
 
 
-def assert_close_rel(got: np.ndarray, ref: np.ndarray, max_rel=1e-2, mean_rel=1e-3):
+def assert_close_rel(got: np.ndarray, ref: np.ndarray, max_rel=2.0 ** -7, mean_rel=2e-4):
     scale = float(np.abs(ref).max()) or 1.0
     diff = np.abs(got.astype(np.float64) - ref.astype(np.float64))
     assert diff.max() <= max_rel * scale, (diff.max(), scale)
