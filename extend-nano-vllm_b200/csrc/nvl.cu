@@ -349,13 +349,18 @@ __global__ void __launch_bounds__(256) nvl_unpack_kernel(
 __global__ void __launch_bounds__(256) nvl_return_kernel(
     const __nv_bfloat16 *__restrict__ y, int hidden, const int32_t *__restrict__ src_rank,
     const int32_t *__restrict__ src_route, const int32_t *__restrict__ route_count,
-    int64_t max_source_routes, int rank, int ep_size, const __grid_constant__ Peers peers, NvlLayout l) {
+    int64_t max_routes, int64_t max_source_routes, int rank, int ep_size,
+    const __grid_constant__ Peers peers, NvlLayout l) {
   pdl_trigger();
   pdl_wait();
   const int lane = threadIdx.x & 31;
   const int warps = blockDim.x >> 5;
   const int vecs = hidden / 8;
-  const int64_t n = *route_count;
+  // More routes than y has rows (a host bound below what the peers sent):
+  // flag it and return only the rows that exist.
+  const int64_t n = min64(max64(*route_count, 0), max_routes);
+  if (blockIdx.x == 0 && threadIdx.x == 0 && *route_count > max_routes)
+    atomicOr(&g_status, kStatusIndex);
   for (int64_t j = int64_t(blockIdx.x) * warps + (threadIdx.x >> 5); j < n;
        j += int64_t(gridDim.x) * warps) {
     const int s = src_rank[j];
@@ -587,7 +592,7 @@ int b200moe_nvl_return(const void *y, int hidden, const int32_t *src_rank,
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   B200_LAUNCH_PDL(kPdlExchange, nvl_return_kernel, dim3(grid_for(max_routes, 8)), dim3(256), 0, s,
                   static_cast<const __nv_bfloat16 *>(y), hidden, src_rank, src_route,
-                  route_count, max_source_routes, rank, ep_size, p, *l);
+                  route_count, max_routes, max_source_routes, rank, ep_size, p, *l);
   B200_LAUNCHED();
   return B200MOE_OK;
 }

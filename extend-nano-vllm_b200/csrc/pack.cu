@@ -148,6 +148,8 @@ __global__ void __launch_bounds__(kPackThreads) pack_scatter_kernel(ScatterArgs 
   const int64_t cap_value = a.capacity_dev ? *a.capacity_dev : a.capacity;
   const int64_t cap = cap_value < 0 ? (int64_t)0x3fffffffffffffffLL : cap_value;
   const int64_t n_routes = routes_in_use(a.num_routes, a.route_count);
+  if (b == 0 && threadIdx.x == 0 && a.route_count && *a.route_count > a.num_routes)
+    atomicOr(&g_status, kStatusIndex);  // more routes than the layout was sized for
 
   for (int i = tid; i < L; i += blockDim.x) gof[i] = -1;
   if (tid < 5) red[tid] = 0;

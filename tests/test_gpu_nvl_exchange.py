@@ -119,18 +119,21 @@ def test_exchange_round_robin_placement():
 
 
 @pytest.mark.parametrize("kw", [{}, {"expert_capacity_factor": 1.25}])
+@pytest.mark.parametrize("counts", [(32, 32, 32, 32), (8, 64, 1, 40)])
 @torch.inference_mode()
-def test_exchange_replays_from_one_cuda_graph(kw):
+def test_exchange_replays_from_one_cuda_graph(kw, counts):
     """All ranks' phases captured into one graph; replays with new inputs
-    (device-side counts, no host reads) equal the single-GPU layer."""
-    world, tokens = 4, 32
+    (device-side counts, no host reads) equal the single-GPU layer.  Ranks
+    may hold different batch sizes in the same captured step: nothing in
+    the exchange needs equal sizes, only the coordinated counts that bound
+    the temporaries."""
+    world = len(counts)
     full, ranks = _layers(world, kw)
-    bufs = _buffers(ranks, tokens)
-    dist_env.set_moe_token_counts((tokens,) * world)
-    xs = [torch.empty((tokens, SHAPE.hidden), device=DEV, dtype=torch.bfloat16)
-          for _ in range(world)]
+    bufs = _buffers(ranks, max(counts))
+    dist_env.set_moe_token_counts(counts)
+    xs = [torch.empty((c, SHAPE.hidden), device=DEV, dtype=torch.bfloat16) for c in counts]
     for r, x in enumerate(xs):
-        x.copy_(wl.hidden_states(tokens, SHAPE.hidden, seed=5 + r))
+        x.copy_(wl.hidden_states(counts[r], SHAPE.hidden, seed=5 + r))
     stream = torch.cuda.Stream()
     stream.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(stream):
@@ -141,7 +144,7 @@ def test_exchange_replays_from_one_cuda_graph(kw):
         outs = _exchange(ranks, bufs, xs)
     for step in range(3):
         for r, x in enumerate(xs):
-            x.copy_(wl.hidden_states(tokens, SHAPE.hidden, seed=100 + 10 * step + r).to(DEV))
+            x.copy_(wl.hidden_states(counts[r], SHAPE.hidden, seed=100 + 10 * step + r).to(DEV))
         graph.replay()
         expected = full(torch.cat(xs))
         torch.cuda.synchronize()

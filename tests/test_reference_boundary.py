@@ -78,6 +78,9 @@ def _worker(port: int, queue) -> None:
         cfg = _config()
         torch.manual_seed(0)
         model = qwen3_moe.Qwen3MoeForCausalLM(cfg).to(torch.bfloat16)
+        with torch.no_grad():
+            for parameter in model.parameters():
+                parameter.normal_(0.0, 0.02)
         moes = [layer.mlp for layer in model.model.layers.values()]
         checks["layers"] = all(type(m) is b2.ExpertParallelMoE for m in moes)
         ref_layer = original(cfg.hidden_size, cfg.moe_intermediate_size, cfg.num_experts,
