@@ -25,6 +25,10 @@ chunked-prefill batch with Zipf(1.2) expert popularity and capacity factor
 CPU algorithm (softmax/top-k and the per-expert torch loop of
 nanovllm/layers/moe.py:546-580, restated in oracle/) on a bounded sample.
 
+At N = 1 the line also carries ``reference_triton_gpu``: the unmodified
+reference's own GPU path (Triton kernels, installed in baseline/_ref) timed
+on the same GPU with the same workloads and timing, and the speed-ups over it.
+
 ``--impl reference`` times that CPU implementation alone on the host cores
 (rank 0 only) on the same workload and prints the same line with
 "impl": "reference".
@@ -88,6 +92,8 @@ def parse_args():
     p.add_argument("--impl", choices=("native", "reference"), default="native")
     p.add_argument("--no-sweep", action="store_true", help="skip the N=1 decode/prefill sweep")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-reference-triton", action="store_true",
+                   help="skip timing the reference's own GPU path (baseline/_ref) at N=1")
     p.add_argument("--profile-case", choices=("gemm-small", "decode", "prefill"), default=None,
                    help="run a case for ncu captures and exit (no JSON line): gemm-small = "
                         "235B-shaped experts, 16 experts x 320 routed rows, 604 MB of "
@@ -517,6 +523,104 @@ def headline_config(shape, world: int) -> dict:
                   % (shape.num_experts // world * shape.expert_bytes / 1e9)}
 
 
+def reference_triton(steps: int, warmup: int) -> dict:
+    """The unmodified reference's own GPU path on this GPU, same workloads and
+    timing as the native lines: its Triton grouped GEMMs, torch routing and
+    packing (nanovllm/layers/moe.py _forward_triton for the 235B headline and
+    the Zipf prefill, _forward_static_decode captured in one CUDA graph per
+    decode bucket, as its model runner does).  Imported from baseline/_ref
+    (baseline/install_reference.sh); a same-box comparison, not the product."""
+    import importlib
+
+    import extend_nano_vllm_b200.workloads as wl
+
+    ref_dir = os.path.join(REPO, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_dir, "nanovllm")):
+        return {"unavailable": "reference not installed in baseline/_ref"}
+    if ref_dir not in sys.path:
+        sys.path.append(ref_dir)
+    try:
+        ref_moe = importlib.import_module("nanovllm.layers.moe")
+    except Exception as exc:  # noqa: BLE001 - reported in the JSON line
+        return {"unavailable": f"reference import failed: {exc!r}"[:300]}
+    device = torch.device("cuda")
+
+    def make(shape, seed_w, seed_g, **kw):
+        layer = ref_moe.ExpertParallelMoE(shape.hidden, shape.intermediate, shape.num_experts,
+                                          shape.top_k, shape.norm_topk_prob, **kw)
+        layer = layer.to(device=device, dtype=torch.bfloat16)
+        w13, w2 = wl.expert_weights(shape, seed=seed_w, device=device, on_device=True)
+        with torch.no_grad():
+            layer.gate.weight.copy_(wl.gate_weight(shape, seed=seed_g).to(device))
+            layer.gate_up_proj.copy_(w13)
+            layer.down_proj.copy_(w2)
+        return layer
+
+    out = {}
+    shape = wl.QWEN3_235B_A22B
+    layer = make(shape, 2024, 2025)
+    x = wl.hidden_states(TOKENS_PER_GPU, shape.hidden, seed=1000, device=device)
+    with torch.no_grad():
+        seconds = time_steps(lambda: layer(x), steps, warmup, 1)
+    ms = seconds / steps * 1e3
+    out["headline_235b_t4096"] = {"ms": round(ms, 4),
+                                  "tokens_per_s": round(TOKENS_PER_GPU / (ms / 1e3), 1)}
+    del layer, x
+    torch.cuda.empty_cache()
+
+    shape = wl.QWEN3_30B_A3B
+    layer = make(shape, 2024, 2025, graph_safe_decode=True)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    flush_read = torch.ones(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    decode = []
+    for tokens in DECODE_BUCKETS:
+        x = wl.hidden_states(tokens, shape.hidden, seed=300 + tokens, device=device)
+        logits = wl.uniform_logits(tokens, shape.num_experts, seed=400 + tokens, device=device)
+        layer.gate.forward = lambda h, _l=logits: _l  # the same injected fp32 logits
+        stream = torch.cuda.Stream()
+        stream.wait_stream(torch.cuda.current_stream())
+        with torch.no_grad(), torch.cuda.stream(stream):
+            for _ in range(3):
+                layer(x)
+        torch.cuda.current_stream().wait_stream(stream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.no_grad(), torch.cuda.graph(graph):
+            layer(x)
+        for _ in range(warmup):
+            graph.replay()
+        times = []
+        for _ in range(max(20, steps // 4)):
+            flush.fill_(1)
+            flush_read.amax()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            graph.replay()
+            b.record()
+            times.append((a, b))
+        torch.cuda.synchronize()
+        ms = statistics.median(a.elapsed_time(b) for a, b in times)
+        decode.append({"tokens": tokens, "ms": round(ms, 5),
+                       "tokens_per_s": round(tokens / (ms / 1e3), 1)})
+        del graph
+    out["decode_30b_a3b"] = decode
+    del layer, flush, flush_read
+    torch.cuda.empty_cache()
+
+    layer = make(shape, 2024, 2025, expert_capacity_factor=1.25)
+    x = wl.hidden_states(PREFILL_TOKENS, shape.hidden, seed=500, device=device)
+    logits = wl.zipf_logits(PREFILL_TOKENS, shape.num_experts, seed=501, device=device)
+    layer.gate.forward = lambda h: logits
+    with torch.no_grad():
+        seconds = time_steps(lambda: layer(x), max(10, steps // 10), warmup, 1)
+    ms = seconds / max(10, steps // 10) * 1e3
+    out["prefill_30b_a3b_zipf"] = {"ms": round(ms, 4),
+                                   "tokens_per_s": round(PREFILL_TOKENS / (ms / 1e3), 1)}
+    del layer
+    torch.cuda.empty_cache()
+    return out
+
+
 def native(args, world, rank, local, json_fd: int = 1) -> None:
     import extend_nano_vllm_b200 as pkg
     import extend_nano_vllm_b200.workloads as wl
@@ -612,6 +716,19 @@ def native(args, world, rank, local, json_fd: int = 1) -> None:
                                                           args.warmup, pk),
                            "prefill_30b_a3b_zipf": prefill_case(max(10, args.steps // 10),
                                                                 args.warmup, pk)}
+        if not args.no_reference_triton:
+            ref = reference_triton(args.steps, args.warmup)
+            record["reference_triton_gpu"] = ref
+            if "headline_235b_t4096" in ref:
+                sweep = record["sweep"]
+                record["speedup_vs_reference_triton_gpu"] = {
+                    "headline_235b_t4096": round(ref["headline_235b_t4096"]["ms"]
+                                                 / ms_per_step, 2),
+                    "prefill_30b_a3b_zipf": round(ref["prefill_30b_a3b_zipf"]["ms"]
+                                                  / sweep["prefill_30b_a3b_zipf"]["ms"], 2),
+                    "decode_30b_a3b": {str(r["tokens"]): round(r["ms"] / n["ms"], 2)
+                                       for r, n in zip(ref["decode_30b_a3b"],
+                                                       sweep["decode_30b_a3b"])}}
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         record["cpu_baseline"] = cpu_config1_baseline(wl)
     if rank == 0:

@@ -336,8 +336,9 @@ class ExpertParallelMoE(nn.Module):
         """Move expert weights between EP ranks in place (moe.py:407-489).
 
         Every rank must request the same placement (agreed with
-        all_gather_object before any data moves).  Weights travel with one
-        all_to_all_single per projection and are copied into the existing
+        all_gather_object before any data moves).  Per projection the rows
+        that leave are gathered with one index_select, travel with one NCCL
+        all_to_all_single and land with one index_copy_ in the existing
         parameter storage, so captured CUDA graphs stay valid.
         """
         if not self.dynamic_placement:
@@ -358,32 +359,33 @@ class ExpertParallelMoE(nn.Module):
         old = self.expert_owners
         new_ids = tuple(e for e, o in enumerate(owners) if o == self.ep_rank)
         new_local = {e: i for i, e in enumerate(new_ids)}
-        # Rows leave in destination order; within a destination in expert order.
+        # Rows leave in destination order, within a destination in expert
+        # order; they arrive in source order, within a source in expert order.
         outgoing = [e for d in range(self.ep_size) for e in self.local_expert_ids if owners[e] == d]
         send_counts = [sum(owners[e] == d for e in self.local_expert_ids)
                        for d in range(self.ep_size)]
         incoming = [e for s in range(self.ep_size) for e in new_ids if old[e] == s]
         recv_counts = [sum(old[e] == s for e in new_ids) for s in range(self.ep_size)]
+        device = self.gate_up_proj.device
+        gather = torch.tensor([self.expert_id_to_local[e] for e in outgoing], device=device)
+        scatter = torch.tensor([new_local[e] for e in incoming], device=device)
 
-        def exchange(param: torch.Tensor) -> torch.Tensor:
-            rows = param[[self.expert_id_to_local[e] for e in outgoing]].contiguous()
-            received = torch.empty_like(rows)
+        def exchange(param: torch.Tensor) -> None:
+            # One gather of the rows that leave, one all-to-all, one scatter
+            # into the same storage (captured graphs keep their pointers).
+            rows = param.index_select(0, gather)
             if self.ep_size > 1:
+                received = torch.empty_like(rows)
                 row = param[0].numel()
                 dist.all_to_all_single(received.view(-1), rows.view(-1),
                                        [c * row for c in recv_counts],
                                        [c * row for c in send_counts], group=group)
             else:
-                received.copy_(rows)
-            reordered = torch.empty_like(param)
-            for i, e in enumerate(incoming):
-                reordered[new_local[e]].copy_(received[i])
-            return reordered
+                received = rows
+            param.index_copy_(0, scatter, received)
 
-        gate_up = exchange(self.gate_up_proj)
-        down = exchange(self.down_proj)
-        self.gate_up_proj.copy_(gate_up)
-        self.down_proj.copy_(down)
+        exchange(self.gate_up_proj)
+        exchange(self.down_proj)
         self.expert_owner_tensor.copy_(torch.tensor(owners, device=self.expert_owner_tensor.device))
         self.expert_local_index_tensor.copy_(torch.tensor(
             [new_local.get(e, -1) for e in range(self.num_experts)],
