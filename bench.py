@@ -102,6 +102,9 @@ def parse_args():
                         "and replayed --steps times; prefill = the T=8192 Zipf prefill "
                         "case, --steps forwards")
     p.add_argument("--profile-tokens", type=int, default=1)
+    p.add_argument("--profile-engine", default="auto",
+                   choices=("auto", "tcgen05-wide", "tcgen05-swap", "tcgen05-pair"),
+                   help="expert engine of the gemm-small profiling case")
     return p.parse_args()
 
 
@@ -142,6 +145,7 @@ def profile_case(args) -> None:
         return
     shape = wl.LayerShape("profile-small", 4096, 1536, 16, 8)
     layer = build_layer(shape, 1, 0, device)
+    layer.expert_engine = args.profile_engine
     x = wl.hidden_states(640, shape.hidden, seed=3, device=device)
     for _ in range(max(1, args.steps)):
         layer(x)
@@ -183,7 +187,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-i", str(self.gpu_index), "-lms", "50"],
+                 "-i", str(self.gpu_index), "-lms", "20"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             time.sleep(0.5)  # let the sampler come up before the timed region
         except OSError:
@@ -205,29 +209,35 @@ class ClockSampler:
         except subprocess.TimeoutExpired:
             self.proc.kill()
             out, _ = self.proc.communicate()
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        slack = datetime.timedelta(milliseconds=50)
+        rows = []
         for line in out.strip().splitlines():
             r = [c.strip() for c in line.split(",")]
             if len(r) < 10:
                 continue
             try:
                 stamp = datetime.datetime.strptime(r[0], "%Y/%m/%d %H:%M:%S.%f")
-                clock, clock_max = float(r[2]), float(r[3])
+                rows.append((stamp, float(r[2]), float(r[3]), r[6:10]))
             except ValueError:
                 continue
-            if self.begin_t and self.end_t and not (
-                    self.begin_t - slack <= stamp <= self.end_t + slack):
-                continue
-            sm.append(clock)
-            mx.append(clock_max)
-            for name, flag in zip(names, r[6:10]):
-                if flag.lower().startswith("active"):
-                    reasons.add(name)
+        # Samples stamped inside the timed region; a region shorter than the
+        # sampling period takes the samples closest to it (within 100 ms).
+        window = "timed region"
+        picked = rows
+        if self.begin_t and self.end_t:
+            slack = datetime.timedelta(milliseconds=20)
+            picked = [x for x in rows if self.begin_t - slack <= x[0] <= self.end_t + slack]
+            if not picked:
+                slack = datetime.timedelta(milliseconds=100)
+                picked = [x for x in rows if self.begin_t - slack <= x[0] <= self.end_t + slack]
+                window = "within 100 ms of the timed region"
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = {name for x in picked for name, flag in zip(names, x[3])
+                   if flag.lower().startswith("active")}
+        sm = [x[1] for x in picked]
+        mx = [x[2] for x in picked]
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "window": window}
 
 
 class KernelTimer:
