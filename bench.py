@@ -708,7 +708,7 @@ def native(args, world, rank, local, json_fd: int = 1) -> None:
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) hidden, N(0,0.02) weights; no checkpoint)",
         "config": headline_config(shape, world),
-        "exchange": "nccl all_to_all_single" if world > 1 else "none",
+        "exchange": "NVLink peer memory (CUDA IPC), graph-safe" if world > 1 else "none",
         "kept_routes_per_gpu_step": round(kept_per_step, 1),
         "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": h2d},
