@@ -101,9 +101,13 @@ def parse_args():
                         "decode bucket of --profile-tokens tokens captured in a CUDA graph "
                         "and replayed --steps times; prefill = the T=8192 Zipf prefill "
                         "case, --steps forwards")
+    p.add_argument("--engine", default="auto",
+                   choices=("auto", "tcgen05", "tcgen05-wide", "tcgen05-tall", "tcgen05-pair"),
+                   help="expert GEMM engine of the headline layer (default: the library's choice)")
     p.add_argument("--profile-tokens", type=int, default=1)
     p.add_argument("--profile-engine", default="auto",
-                   choices=("auto", "tcgen05-wide", "tcgen05-swap", "tcgen05-pair"),
+                   choices=("auto", "tcgen05-wide", "tcgen05-swap", "tcgen05-pair",
+                            "tcgen05-tall"),
                    help="expert engine of the gemm-small profiling case")
     return p.parse_args()
 
@@ -640,6 +644,7 @@ def native(args, world, rank, local, json_fd: int = 1) -> None:
     shape = wl.QWEN3_235B_A22B
     device = torch.device("cuda", local)
     layer = build_layer(shape, world, rank, device)
+    layer.expert_engine = args.engine
     x = wl.hidden_states(TOKENS_PER_GPU, shape.hidden, seed=1000 + rank, device=device)
     step = lambda: layer(x)  # noqa: E731
 

@@ -22,6 +22,7 @@ EUNSUPPORTED = 3
 BF16, F16, F32, F64 = 0, 1, 2, 3
 ENGINE_STREAM, ENGINE_TCGEN05, ENGINE_TCGEN05_WIDE, ENGINE_TCGEN05_SWAP = 0, 1, 2, 3
 ENGINE_TCGEN05_PAIR = 4
+ENGINE_TCGEN05_TALL = 5
 MTILE_WORDS = 3
 MTILE_ROWS = 128
 CHUNK_ROWS = 256

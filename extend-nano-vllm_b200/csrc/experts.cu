@@ -26,6 +26,14 @@ int tcs_down(const void *act, int hidden, int inter, const void *w2, int num_loc
              const int32_t *row_route, const void *route_weights, int64_t num_routes,
              int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
              const int32_t *counters, void *y, cudaStream_t s);
+int tct_gate_up(const void *x_packed, int hidden, int inter, const void *w13, int num_local,
+                int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
+                const int32_t *counters, void *act, cudaStream_t s);
+int tct_down(const void *act, int hidden, int inter, const void *w2, int num_local,
+             const int32_t *row_route, const void *route_weights, int64_t num_routes,
+             int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
+             const int32_t *counters, void *y, cudaStream_t s);
+bool tall_fits(int64_t max_mtiles);
 int tcp_gate_up(const void *x_packed, int hidden, int inter, const void *w13, int num_local,
                 int64_t row_capacity, const int32_t *chunks, int64_t max_chunks,
                 const int32_t *counters, void *act, cudaStream_t s);
@@ -65,6 +73,14 @@ int b200moe_expert_gate_up(int engine, const void *x, int64_t x_rows, const void
   B200_ARG(aligned16(w13) && aligned16(act), "w13 and act must be 16-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   engine = resolve_engine(engine, num_routes);
+  if (engine == B200MOE_ENGINE_TCGEN05_TALL) {
+    // 256-row tiles read a packed copy of the rows; without one, or beyond
+    // the work list it holds, the wide tiles run instead (same results).
+    if (x_packed != nullptr && aligned16(x_packed) && tall_fits(max_mtiles))
+      return tct_gate_up(x_packed, hidden, inter, w13, num_local_experts, row_capacity, mtiles,
+                         max_mtiles, counters, act, s);
+    engine = B200MOE_ENGINE_TCGEN05_WIDE;
+  }
   if (engine == B200MOE_ENGINE_STREAM) {
     B200_ARG(x != nullptr && aligned16(x), "x must be a 16-byte aligned device pointer");
     return stream_gate_up(x, x_rows, hidden, inter, w13, row_route, token_of_route, top_k,
@@ -119,6 +135,12 @@ int b200moe_expert_down(int engine, const void *act, int hidden, int inter, cons
   B200_ARG(aligned16(act) && aligned16(w2) && aligned16(y), "act, w2, y must be 16-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   engine = resolve_engine(engine, num_routes);
+  if (engine == B200MOE_ENGINE_TCGEN05_TALL) {
+    if (tall_fits(max_mtiles))
+      return tct_down(act, hidden, inter, w2, num_local_experts, row_route, route_weights,
+                      num_routes, row_capacity, mtiles, max_mtiles, counters, y, s);
+    engine = B200MOE_ENGINE_TCGEN05_WIDE;
+  }
   if (engine == B200MOE_ENGINE_STREAM)
     return stream_down(act, hidden, inter, w2, row_route, route_weights, num_routes,
                        max_expert_rows, mtiles, max_mtiles, counters, y, s);

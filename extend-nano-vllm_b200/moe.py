@@ -224,8 +224,8 @@ class ExpertParallelMoE(nn.Module):
         # functions to exercise the host logic without a GPU.
         self._ops = _native_ops
         # "auto" | "stream" | "tcgen05" | "tcgen05-wide" | "tcgen05-swap" |
-        # "tcgen05-pair": expert GEMM engine ("tcgen05" lets the library pick
-        # the variant per call).
+        # "tcgen05-pair" | "tcgen05-tall": expert GEMM engine ("tcgen05" lets
+        # the library pick the variant per call).
         self.expert_engine = "auto"
         # Optional object with begin(name)/end(name) that records CUDA events
         # around the grouped GEMM launches (used by the benchmark).
@@ -470,6 +470,8 @@ class ExpertParallelMoE(nn.Module):
             return _lib.ENGINE_TCGEN05_SWAP
         if self.expert_engine == "tcgen05-pair":
             return _lib.ENGINE_TCGEN05_PAIR
+        if self.expert_engine == "tcgen05-tall":
+            return _lib.ENGINE_TCGEN05_TALL
         if self.expert_engine != "auto":
             raise ValueError(f"unknown expert engine {self.expert_engine!r}")
         return _lib.ENGINE_STREAM if num_routes <= STREAM_ENGINE_MAX_ROUTES else _lib.ENGINE_TCGEN05

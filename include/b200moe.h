@@ -52,6 +52,9 @@ extern "C" {
                                         128/256-wide weight tiles as N */
 #define B200MOE_ENGINE_TCGEN05_SWAP 3 /* weight rows as the MMA M operand (128 features),
                                         routed rows as N (rounded to 16) */
+#define B200MOE_ENGINE_TCGEN05_TALL 5 /* 256 routed rows of one expert per work item: two
+                                        M=128 MMAs share each staged 256-wide weight tile
+                                        (needs x_packed; otherwise runs WIDE) */
 #define B200MOE_ENGINE_TCGEN05_PAIR 4 /* two-SM (cta_group::2) swap-AB: 256 weight rows as M,
                                         row chunks of <= 256 routed rows as N; needs the
                                         `chunks` list of b200moe_pack_routes */

@@ -215,7 +215,7 @@ def _expert_case(shape, tokens, engine, seed, logits_kind="uniform", capacity=No
                         capacity=capacity)
     if engine == _lib.ENGINE_STREAM:
         act = ops.expert_gate_up(engine, xd, None, w13d, p, shape.top_k)
-    elif packed_rows or engine == _lib.ENGINE_TCGEN05_PAIR:
+    elif packed_rows or engine in (_lib.ENGINE_TCGEN05_PAIR, _lib.ENGINE_TCGEN05_TALL):
         xp = ops.gather_rows(xd, p, shape.top_k)
         act = ops.expert_gate_up(engine, xd, xp, w13d, p, shape.top_k)
     else:
@@ -237,9 +237,9 @@ A = wl.QWEN3_30B_A3B
 
 
 ENGINES = [_lib.ENGINE_STREAM, _lib.ENGINE_TCGEN05, _lib.ENGINE_TCGEN05_WIDE,
-           _lib.ENGINE_TCGEN05_SWAP, _lib.ENGINE_TCGEN05_PAIR]
+           _lib.ENGINE_TCGEN05_SWAP, _lib.ENGINE_TCGEN05_PAIR, _lib.ENGINE_TCGEN05_TALL]
 TC_ENGINES = [_lib.ENGINE_TCGEN05, _lib.ENGINE_TCGEN05_WIDE, _lib.ENGINE_TCGEN05_SWAP,
-              _lib.ENGINE_TCGEN05_PAIR]
+              _lib.ENGINE_TCGEN05_PAIR, _lib.ENGINE_TCGEN05_TALL]
 
 
 @pytest.mark.parametrize("engine", ENGINES)
@@ -272,6 +272,21 @@ def test_fused_row_gather_equals_packed_copy(engine, shape, tokens):
     fused = _expert_case(shape, tokens, engine, seed=200 + tokens)
     packed = _expert_case(shape, tokens, engine, seed=200 + tokens, packed_rows=True)
     assert torch.equal(fused, packed)
+
+
+@pytest.mark.parametrize("shape,tokens,kind", [
+    (SMALL, 1100, "uniform"), (SMALL, 2048, "zipf"), (A, 2048, "zipf"), (A, 640, "uniform"),
+    (wl.LayerShape("d-16", 4096, 1536, 16, 8), 640, "uniform"),
+    (wl.LayerShape("d-32", 4096, 1536, 32, 8), 1100, "zipf")])
+def test_tall_tiles_equal_wide_tiles_bit_for_bit(shape, tokens, kind):
+    """256-row work items (two M=128 MMAs on one staged weight tile) compute
+    every output element with the same K order as 128-row tiles: the same
+    bits, for experts of every size (odd and even tile counts, remainders)."""
+    tall = _expert_case(shape, tokens, _lib.ENGINE_TCGEN05_TALL, seed=40 + tokens,
+                        logits_kind=kind)
+    wide = _expert_case(shape, tokens, _lib.ENGINE_TCGEN05_WIDE, seed=40 + tokens,
+                        logits_kind=kind, packed_rows=True)
+    assert torch.equal(tall, wide)
 
 
 @pytest.mark.parametrize("tokens,top_k,ep_size", [(1, 8, 2), (300, 8, 4), (4096, 8, 8),

@@ -117,6 +117,8 @@ CASES = [
     ("d235b_T512_pair", wl.QWEN3_235B_A22B, 512, "gate", None, "tcgen05-pair"),
     ("d235b_T4096_wide", wl.QWEN3_235B_A22B, 4096, "gate", None, "auto"),
     ("d235b_T4096_pair", wl.QWEN3_235B_A22B, 4096, "gate", None, "tcgen05-pair"),
+    ("d235b_T4096_tall", wl.QWEN3_235B_A22B, 4096, "gate", None, "tcgen05-tall"),
+    ("a30b_T8192_zipf_cap_tall", wl.QWEN3_30B_A3B, 8192, "zipf", 1.25, "tcgen05-tall"),
 ]
 
 
