@@ -456,6 +456,92 @@ def decode_sweep(steps: int, warmup: int, pk: dict) -> list[dict]:
     return results
 
 
+# Token counts of the reference's shared-expert benchmark
+# (benchmarks/bench_moe_shared.py: --tokens 16 | 32).
+SHARED_BUCKETS = (16, 32)
+
+
+def graph_latency_ms(forward, steps: int, warmup: int, flush, flush_read) -> float:
+    """Median device time of one CUDA-graph replay of ``forward()`` with L2
+    flushed (write then read 256 MB) before each replay."""
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.no_grad(), torch.cuda.stream(stream):
+        for _ in range(3):
+            forward()
+    torch.cuda.current_stream().wait_stream(stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.no_grad(), torch.cuda.graph(graph):
+        forward()
+    for _ in range(warmup):
+        graph.replay()
+    times = []
+    for _ in range(steps):
+        flush.fill_(1)
+        flush_read.amax()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        graph.replay()
+        b.record()
+        times.append((a, b))
+    torch.cuda.synchronize()
+    del graph
+    return statistics.median(a.elapsed_time(b) for a, b in times)
+
+
+def load_shared_layer(layer, shape, device) -> None:
+    import extend_nano_vllm_b200.workloads as wl
+    w13, w2 = wl.expert_weights(shape, seed=2024, device=device, on_device=True)
+    s13, s2, sg = wl.shared_expert_weights(shape, seed=2024, device=device)
+    with torch.no_grad():
+        layer.gate.weight.copy_(wl.gate_weight(shape, seed=2025).to(device))
+        layer.gate_up_proj.copy_(w13)
+        layer.down_proj.copy_(w2)
+        layer.shared_expert.gate_up_proj.weight.copy_(s13)
+        layer.shared_expert.down_proj.weight.copy_(s2)
+        layer.shared_expert_gate.weight.copy_(sg)
+
+
+def shared_expert_sweep(steps: int, warmup: int, pk: dict) -> dict:
+    """Qwen3-Next-shaped layer with a shared expert (512 experts, top-10,
+    routed and shared width 512), decode graphs at the reference benchmark's
+    token counts: the shared expert inside the grouped expert launches
+    ("fused") against the same layer computing it after the routed output
+    with torch, as the reference does ("unfused")."""
+    import extend_nano_vllm_b200.workloads as wl
+    from extend_nano_vllm_b200.moe import ExpertParallelMoE
+
+    shape = wl.QWEN3_NEXT_80B_A3B
+    device = torch.device("cuda")
+    layer = ExpertParallelMoE(shape.hidden, shape.intermediate, shape.num_experts, shape.top_k,
+                              shape.norm_topk_prob, graph_safe_decode=True,
+                              shared_expert_intermediate_size=shape.shared_intermediate)
+    layer = layer.to(device=device, dtype=torch.bfloat16)
+    load_shared_layer(layer, shape, device)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    flush_read = torch.ones(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    rows = []
+    for tokens in SHARED_BUCKETS:
+        x = wl.hidden_states(tokens, shape.hidden, seed=71 + tokens, device=device)
+        row = {"tokens": tokens}
+        for fused in (True, False):
+            layer.fuse_shared_expert = fused
+            ms = graph_latency_ms(lambda: layer(x), steps, warmup, flush, flush_read)
+            row["ms_fused" if fused else "ms_unfused"] = round(ms, 5)
+        ids = torch.topk(layer.gate(x), shape.top_k, dim=-1).indices
+        active = int(torch.unique(ids).numel()) + 1
+        bytes_ = active * shape.expert_bytes + tokens * shape.hidden * 2 * 2
+        row["active_experts_incl_shared"] = active
+        row["hbm_roofline_frac_fused"] = round(
+            bytes_ / (row["ms_fused"] / 1e3) / 1e9 / pk["hbm_gbs"], 4)
+        rows.append(row)
+    layer.fuse_shared_expert = True
+    del layer, flush, flush_read
+    torch.cuda.empty_cache()
+    return {"shape": shape.name, "buckets": rows}
+
+
 def prefill_case(steps: int, warmup: int, pk: dict) -> dict:
     import extend_nano_vllm_b200.workloads as wl
 
@@ -632,6 +718,25 @@ def reference_triton(steps: int, warmup: int) -> dict:
                                    "tokens_per_s": round(PREFILL_TOKENS / (ms / 1e3), 1)}
     del layer
     torch.cuda.empty_cache()
+
+    # The reference's shared-expert benchmark shape (bench_moe_shared.py):
+    # its layer with graph-safe decode and the shared expert, same weights.
+    shape = wl.QWEN3_NEXT_80B_A3B
+    layer = ref_moe.ExpertParallelMoE(
+        shape.hidden, shape.intermediate, shape.num_experts, shape.top_k, shape.norm_topk_prob,
+        graph_safe_decode=True, shared_expert_intermediate_size=shape.shared_intermediate)
+    layer = layer.to(device=device, dtype=torch.bfloat16)
+    load_shared_layer(layer, shape, device)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    flush_read = torch.ones(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    rows = []
+    for tokens in SHARED_BUCKETS:
+        x = wl.hidden_states(tokens, shape.hidden, seed=71 + tokens, device=device)
+        ms = graph_latency_ms(lambda: layer(x), max(20, steps // 4), warmup, flush, flush_read)
+        rows.append({"tokens": tokens, "ms": round(ms, 5)})
+    out["shared_next_decode"] = rows
+    del layer, flush, flush_read
+    torch.cuda.empty_cache()
     return out
 
 
@@ -734,7 +839,9 @@ def native(args, world, rank, local, json_fd: int = 1) -> None:
         record["sweep"] = {"decode_30b_a3b": decode_sweep(max(20, args.steps // 4),
                                                           args.warmup, pk),
                            "prefill_30b_a3b_zipf": prefill_case(max(10, args.steps // 10),
-                                                                args.warmup, pk)}
+                                                                args.warmup, pk),
+                           "shared_expert_next": shared_expert_sweep(max(20, args.steps // 4),
+                                                                     args.warmup, pk)}
         if not args.no_reference_triton:
             ref = reference_triton(args.steps, args.warmup)
             record["reference_triton_gpu"] = ref
@@ -747,7 +854,11 @@ def native(args, world, rank, local, json_fd: int = 1) -> None:
                                                   / sweep["prefill_30b_a3b_zipf"]["ms"], 2),
                     "decode_30b_a3b": {str(r["tokens"]): round(r["ms"] / n["ms"], 2)
                                        for r, n in zip(ref["decode_30b_a3b"],
-                                                       sweep["decode_30b_a3b"])}}
+                                                       sweep["decode_30b_a3b"])},
+                    "shared_next_decode": {
+                        str(r["tokens"]): round(r["ms"] / n["ms_fused"], 2)
+                        for r, n in zip(ref.get("shared_next_decode", []),
+                                        sweep["shared_expert_next"]["buckets"])}}
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         record["cpu_baseline"] = cpu_config1_baseline(wl)
     if rank == 0:

@@ -41,11 +41,14 @@ SIGNATURES: dict[str, tuple] = {
     "b200moe_abi_version": (_I, []),
     "b200moe_device_status": (_I, [_P, _I]),
     "b200moe_route_topk": (_I, [_P, _I, _L, _I, _I, _I, _P, _P, _P]),
+    "b200moe_route_topk_shared": (_I, [_P, _I, _L, _I, _I, _I, _P, _P, _P, _P]),
     "b200moe_pack_scratch_bytes": (_S, [_L, _I]),
     "b200moe_pack_row_capacity": (_L, [_L, _I]),
     "b200moe_pack_max_mtiles": (_L, [_L, _I]),
     "b200moe_pack_routes": (_I, [_P, _P, _L, _I, _P, _I, _I, _P, _L, _L, _P, _P, _P, _P, _P,
                                  _P, _P, _L, _P, _P, _P, _P, _S, _P]),
+    "b200moe_pack_routes_shared": (_I, [_P, _P, _L, _I, _I, _P, _I, _I, _L, _L, _P, _P, _P, _P,
+                                        _P, _P, _P, _L, _P, _P, _P, _P, _S, _P]),
     "b200moe_pack_static_scratch_capacity": (_S, []),
     "b200moe_pack_routes_static_scratch": (_I, [_P, _P, _L, _I, _P, _I, _I, _P, _L, _L, _P, _P,
                                                 _P, _P, _P, _P, _P, _L, _P, _P, _P]),
@@ -123,7 +126,8 @@ _NO_KERNEL = ("b200moe_device_status", "b200moe_ipc_handle", "b200moe_ipc_open",
 def _kernels_launched(name: str, args: tuple) -> int:
     if name in _NO_KERNEL:
         return 0
-    if name in ("b200moe_pack_routes", "b200moe_pack_routes_static_scratch"):
+    if name in ("b200moe_pack_routes", "b200moe_pack_routes_static_scratch",
+                "b200moe_pack_routes_shared"):
         routes = int(args[2])
         return 0 if routes == 0 else 1 if routes <= PACK_SINGLE_LAUNCH_ROUTES else 2
     if name == "b200moe_decode_tiny":

@@ -95,6 +95,10 @@ struct ScatterArgs {
   int num_local;
   const int32_t *expert_base;
   int64_t capacity;  // < 0: unlimited
+  // Experts [capped_experts, num_experts) have no capacity limit and are left
+  // out of the kept/dropped counts (shared experts appended to the routed
+  // ones); capped_experts == num_experts otherwise.
+  int capped_experts;
   const int64_t *capacity_dev;  // device-side capacity (overrides capacity) or null
   const int32_t *route_count;   // device-side number of routes in use, or null
   int64_t row_capacity;
@@ -212,7 +216,7 @@ __global__ void __launch_bounds__(kPackThreads) pack_scatter_kernel(ScatterArgs 
       int64_t kept = 0;
       if (g >= 0) {
         const int64_t eb = a.expert_base ? a.expert_base[g] : 0;
-        kept = min64(tot[g], max64(0, cap - eb));
+        kept = g < a.capped_experts ? min64(tot[g], max64(0, cap - eb)) : tot[g];
       }
       lkept[l] = static_cast<int32_t>(kept);
       rows += (kept + B200MOE_BLOCK_ROWS - 1) / B200MOE_BLOCK_ROWS * B200MOE_BLOCK_ROWS;
@@ -329,7 +333,8 @@ __global__ void __launch_bounds__(kPackThreads) pack_scatter_kernel(ScatterArgs 
       int32_t rr = row_sentinel, cr = route_sentinel;
       if (key < E) {
         const int64_t eb = a.expert_base ? a.expert_base[key] : 0;
-        if (eb + pos >= cap) {
+        const bool capped = key < a.capped_experts;
+        if (capped && eb + pos >= cap) {
           a.ids[r] = E;
           if (a.weights) a.weights[r] = __float2bfloat16_rn(0.f);
           ++my_dropped;
@@ -341,7 +346,7 @@ __global__ void __launch_bounds__(kPackThreads) pack_scatter_kernel(ScatterArgs 
               a.row_route[p] = static_cast<int32_t>(r);
               rr = static_cast<int32_t>(p);
               cr = static_cast<int32_t>(r);
-              ++my_kept;
+              my_kept += capped;
             } else {
               atomicOr(&g_status, kStatusIndex);
             }
@@ -398,7 +403,8 @@ size_t scatter_smem_bytes(int num_experts, int num_local) {
 }  // namespace b200moe
 
 static int pack_routes_impl(int64_t *expert_ids, void *route_weights, int64_t num_routes,
-                            int num_experts, const int64_t *local_index, int expert_start,
+                            int num_experts, int num_shared_experts,
+                            const int64_t *local_index, int expert_start,
                             int num_local_experts, const int32_t *expert_base, int64_t capacity,
                             const int64_t *capacity_dev, const int32_t *route_count,
                             int64_t row_capacity, int32_t *row_route, int32_t *route_row,
@@ -412,6 +418,8 @@ static int pack_routes_impl(int64_t *expert_ids, void *route_weights, int64_t nu
   B200_ARG(num_local_experts >= 1 && num_local_experts <= num_experts,
            "num_local_experts must be in [1, num_experts]");
   B200_ARG(counters != nullptr && expert_offsets && expert_counts, "null output pointer");
+  B200_ARG(num_shared_experts >= 0 && num_shared_experts < num_experts,
+           "num_shared_experts must be in [0, num_experts)");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (num_routes == 0) {
     B200_CUDA(cudaMemsetAsync(counters, 0, sizeof(int32_t) * B200MOE_NUM_COUNTERS, s));
@@ -449,6 +457,7 @@ static int pack_routes_impl(int64_t *expert_ids, void *route_weights, int64_t nu
   a.num_local = num_local_experts;
   a.expert_base = expert_base;
   a.capacity = capacity;
+  a.capped_experts = num_experts - num_shared_experts;
   a.capacity_dev = capacity_dev;
   a.route_count = route_count;
   a.row_capacity = row_capacity;
@@ -503,7 +512,7 @@ int b200moe_pack_routes(int64_t *expert_ids, void *route_weights, int64_t num_ro
                         int32_t *expert_counts, int32_t *mtiles, int64_t max_mtiles,
                         int32_t *chunks, int32_t *counters, int64_t *stats, void *scratch,
                         size_t scratch_bytes, void *stream) {
-  return pack_routes_impl(expert_ids, route_weights, num_routes, num_experts, local_index,
+  return pack_routes_impl(expert_ids, route_weights, num_routes, num_experts, 0, local_index,
                           expert_start, num_local_experts, expert_base, capacity, nullptr,
                           nullptr, row_capacity, row_route, route_row, combine_rows,
                           tile_expert, expert_offsets, expert_counts, mtiles, max_mtiles, chunks,
@@ -518,11 +527,28 @@ int b200moe_pack_routes_device_bounds(
     int32_t *tile_expert, int32_t *expert_offsets, int32_t *expert_counts, int32_t *mtiles,
     int64_t max_mtiles, int32_t *chunks, int32_t *counters, int64_t *stats, void *scratch,
     size_t scratch_bytes, void *stream) {
-  return pack_routes_impl(expert_ids, route_weights, num_routes, num_experts, local_index,
+  return pack_routes_impl(expert_ids, route_weights, num_routes, num_experts, 0, local_index,
                           expert_start, num_local_experts, expert_base, capacity, capacity_dev,
                           route_count, row_capacity, row_route, route_row, combine_rows,
                           tile_expert, expert_offsets, expert_counts, mtiles, max_mtiles, chunks,
                           counters, stats, scratch, scratch_bytes, stream);
+}
+
+int b200moe_pack_routes_shared(int64_t *expert_ids, void *route_weights, int64_t num_routes,
+                               int num_experts, int num_shared_experts,
+                               const int64_t *local_index, int expert_start,
+                               int num_local_experts, int64_t capacity, int64_t row_capacity,
+                               int32_t *row_route, int32_t *route_row, int32_t *combine_rows,
+                               int32_t *tile_expert, int32_t *expert_offsets,
+                               int32_t *expert_counts, int32_t *mtiles, int64_t max_mtiles,
+                               int32_t *chunks, int32_t *counters, int64_t *stats,
+                               void *scratch, size_t scratch_bytes, void *stream) {
+  return pack_routes_impl(expert_ids, route_weights, num_routes, num_experts,
+                          num_shared_experts, local_index, expert_start, num_local_experts,
+                          nullptr, capacity, nullptr, nullptr, row_capacity, row_route,
+                          route_row, combine_rows, tile_expert, expert_offsets, expert_counts,
+                          mtiles, max_mtiles, chunks, counters, stats, scratch, scratch_bytes,
+                          stream);
 }
 
 int b200moe_expert_histogram(const int64_t *expert_ids, int64_t num_routes, int num_experts,

@@ -88,13 +88,34 @@ class ReplicatedGate(nn.Module):
         return F.linear(x, self.weight)
 
 
+class SharedMergedGate(ReplicatedGate):
+    """The shared expert's merged gate/up projection [2 * I_s, H]: gate rows
+    first; its loader takes the shard id (0 gate, 1 up) like the reference's
+    SharedMergedReplicatedLinear (moe.py:195-209)."""
+
+    def __init__(self, hidden_size: int, intermediate_size: int) -> None:
+        self.intermediate_size = intermediate_size
+        super().__init__(hidden_size, 2 * intermediate_size)
+
+    def weight_loader(self, param: nn.Parameter, loaded_weight: torch.Tensor,
+                      loaded_shard_id: int | None = None) -> None:
+        if loaded_shard_id is None:
+            param.data.copy_(loaded_weight)
+            return
+        param.data.narrow(0, int(loaded_shard_id) * self.intermediate_size,
+                          self.intermediate_size).copy_(loaded_weight)
+
+
 class SharedExpertMLP(nn.Module):
-    """Dense shared expert (moe.py:212-234), replicated; computed with torch."""
+    """Dense shared expert (moe.py:212-234), replicated.  With one EP rank and
+    the routed experts' width the layer runs it inside the grouped expert
+    kernels; otherwise it is computed as the reference does, after the
+    routed output."""
 
     def __init__(self, hidden_size: int, intermediate_size: int) -> None:
         super().__init__()
         self.intermediate_size = intermediate_size
-        self.gate_up_proj = ReplicatedGate(hidden_size, 2 * intermediate_size)
+        self.gate_up_proj = SharedMergedGate(hidden_size, intermediate_size)
         self.down_proj = ReplicatedGate(intermediate_size, hidden_size)
 
     def forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
@@ -219,6 +240,16 @@ class ExpertParallelMoE(nn.Module):
         self.shared_expert_gate = (
             ReplicatedGate(hidden_size, 1) if shared_expert_intermediate_size is not None
             else None)
+        # A shared expert as wide as the routed experts runs as one more
+        # expert of the grouped GEMMs: its weights sit right after the local
+        # experts' in one storage per projection, and the parameters
+        # (gate_up_proj, down_proj, shared_expert.*.weight) are views of it.
+        self._shared_in_store = shared_expert_intermediate_size == intermediate_size
+        if self._shared_in_store:
+            self._bind_shared_store()
+        # False: compute the shared expert after the routed output, as the
+        # reference does, even where the fused form applies.
+        self.fuse_shared_expert = True
 
         # Kernel entry points; tests may substitute an object with the same
         # functions to exercise the host logic without a GPU.
@@ -244,6 +275,72 @@ class ExpertParallelMoE(nn.Module):
         # (synchronising) on access.
         self._host_counts = {"dispatch": 0, "return": 0, "dropped": 0, "tokens": 0}
         self._stats: torch.Tensor | None = None
+
+    # ------------------------------------------------------------------
+    # Shared expert storage.
+    # ------------------------------------------------------------------
+    def _shared_pairs(self):
+        return ((self.gate_up_proj, self.shared_expert.gate_up_proj.weight),
+                (self.down_proj, self.shared_expert.down_proj.weight))
+
+    def _shares_store(self, routed: torch.Tensor, shared: torch.Tensor) -> bool:
+        if not (routed.is_contiguous() and shared.is_contiguous()
+                and routed.device == shared.device and routed.dtype == shared.dtype):
+            return False
+        if routed.device.type == "meta":
+            return False
+        if routed.untyped_storage().data_ptr() != shared.untyped_storage().data_ptr():
+            return False
+        return shared.data_ptr() == routed.data_ptr() + routed.numel() * routed.element_size()
+
+    def _bind_shared_store(self) -> None:
+        """Re-home the routed and shared weights into one [E_loc + 1, ...]
+        storage per projection (shared expert last) unless they already share
+        one; parameters keep their identity (only ``.data`` changes)."""
+        num_local = self.num_local_experts
+        for routed, shared in self._shared_pairs():
+            if self._shares_store(routed, shared):
+                continue
+            store = torch.empty((num_local + 1, *routed.shape[1:]), device=routed.device,
+                                dtype=routed.dtype)
+            if routed.device.type != "meta":
+                with torch.no_grad():
+                    store[:num_local].copy_(routed.detach())
+                    store[num_local].copy_(shared.detach())
+            routed.data = store[:num_local]
+            shared.data = store[num_local]
+
+    def _apply(self, fn, recurse=True):
+        # Device and dtype moves rebuild every parameter separately; put the
+        # shared expert back behind the routed experts afterwards.
+        super()._apply(fn, recurse)
+        if getattr(self, "_shared_in_store", False):
+            self._bind_shared_store()
+        return self
+
+    def _shared_store(self) -> tuple[torch.Tensor, torch.Tensor]:
+        """[E_loc + 1, 2I, H] and [E_loc + 1, H, I] views over the routed and
+        shared expert weights."""
+        if _capturing():
+            pairs_ok = all(self._shares_store(r, s) for r, s in self._shared_pairs())
+            if not pairs_ok:
+                raise RuntimeError("shared-expert storage was split; run one eager forward "
+                                   "before capturing")
+        else:
+            self._bind_shared_store()
+        out = []
+        for routed, _ in self._shared_pairs():
+            size = (routed.size(0) + 1, *routed.shape[1:])
+            out.append(routed.detach().as_strided(size, routed.stride(), routed.storage_offset()))
+        return out[0], out[1]
+
+    def _fused_shared(self, x: torch.Tensor) -> bool:
+        """The shared expert runs inside the grouped expert path: same width
+        as the routed experts, one EP rank (with several, the reference adds
+        it once per rank after the exchange), the native kernels."""
+        return (self.shared_expert is not None and getattr(self, "_shared_in_store", False)
+                and self.fuse_shared_expert and self.ep_size == 1 and self._ops is _native_ops and x.is_cuda
+                and self.top_k < 32)
 
     # ------------------------------------------------------------------
     # Counters (moe.py:384-393).  Kernels accumulate local assignments and
@@ -478,13 +575,17 @@ class ExpertParallelMoE(nn.Module):
 
     def _run_experts(self, x: torch.Tensor, flat_weights: torch.Tensor, packed, top_k: int,
                      token_of_route: torch.Tensor | None = None,
-                     routes_hint: int | None = None) -> torch.Tensor:
+                     routes_hint: int | None = None,
+                     weights: tuple[torch.Tensor, torch.Tensor] | None = None) -> torch.Tensor:
         """Grouped gate/up + SwiGLU and grouped down -> y [num_routes, H] (route order).
 
         ``routes_hint``: the expected number of routes when ``packed`` is
         bounded on the device (its host num_routes is then only a maximum);
         it picks the tcgen05 variant and the row-gather strategy, and the
-        streaming engine (whose route bound is compiled in) is not used."""
+        streaming engine (whose route bound is compiled in) is not used.
+        ``weights``: (w13, w2) to use instead of the local experts' (the
+        routed + shared storage)."""
+        w13, w2 = (self.gate_up_proj, self.down_proj) if weights is None else weights
         routes = packed.num_routes if routes_hint is None else max(1, int(routes_hint))
         engine = self._engine(routes)
         if routes_hint is not None and engine in (_lib.ENGINE_STREAM, _lib.ENGINE_TCGEN05):
@@ -503,12 +604,11 @@ class ExpertParallelMoE(nn.Module):
             x_packed = ops.gather_rows(x, packed, top_k, token_of_route)
         if timer is not None:
             timer.begin("gate_up")
-        act = ops.expert_gate_up(engine, x, x_packed, self.gate_up_proj, packed, top_k,
-                                 token_of_route)
+        act = ops.expert_gate_up(engine, x, x_packed, w13, packed, top_k, token_of_route)
         if timer is not None:
             timer.end("gate_up")
             timer.begin("down")
-        y = ops.expert_down(engine, act, self.down_proj, packed, flat_weights, x.size(0))
+        y = ops.expert_down(engine, act, w2, packed, flat_weights, x.size(0))
         if timer is not None:
             timer.end("down")
         return y
@@ -580,13 +680,15 @@ class ExpertParallelMoE(nn.Module):
     # ------------------------------------------------------------------
     # Forward.
     # ------------------------------------------------------------------
-    def _forward_local(self, x: torch.Tensor) -> torch.Tensor:
-        """Route + capacity + local experts + combine, no host synchronisation."""
+    def _forward_local(self, x: torch.Tensor, shared: bool = False) -> torch.Tensor:
+        """Route + capacity + local experts + combine, no host synchronisation.
+        ``shared``: include the shared expert (one more grouped expert)."""
         if x.size(0) == 0:
             return torch.zeros_like(x)
-        return self._forward_from_logits(x, self.gate(x))
+        return self._forward_from_logits(x, self.gate(x), shared=shared)
 
-    def _forward_from_logits(self, x: torch.Tensor, logits: torch.Tensor) -> torch.Tensor:
+    def _forward_from_logits(self, x: torch.Tensor, logits: torch.Tensor,
+                             shared: bool = False) -> torch.Tensor:
         """The expert path from given router logits [T, E] (fp32, bf16 or fp16):
         softmax top-k, capacity, packing, grouped GEMMs and combine."""
         num_tokens = x.size(0)
@@ -594,6 +696,8 @@ class ExpertParallelMoE(nn.Module):
             return torch.zeros_like(x)
         self._check_inputs(x)
         stats = self._device_stats(x.device)
+        if shared:
+            return self._forward_with_shared(x, logits, stats)
         if self._use_tiny_path(num_tokens, logits):
             local_index = (self.expert_local_index_tensor if self.expert_id_to_local is not None
                            else None)
@@ -610,9 +714,37 @@ class ExpertParallelMoE(nn.Module):
         self.total_assignment_count += ids.numel()
         return self._combine_expert_routes(y, packed.combine_rows, num_tokens, self.top_k)
 
+    def _forward_with_shared(self, x: torch.Tensor, logits: torch.Tensor,
+                             stats: torch.Tensor | None) -> torch.Tensor:
+        """Routed experts and the shared expert in one grouped expert path.
+
+        The reference adds the shared expert after the routed output
+        (moe.py:1259-1262: output + sigmoid(shared_expert_gate(x)) *
+        shared_expert(x), with the MLP of moe.py:212-234).  Here every token
+        gets a (top_k + 1)-th route to expert E (the shared expert, stored
+        after the local experts) weighted by the bf16 sigmoid of its gate
+        logit; capacity applies to the routed slots only, so routing, packing
+        of the routed experts and drops are unchanged; the down epilogue
+        applies the gate weight in fp32 and the route-order combine adds the
+        shared row after the routed ones."""
+        num_tokens = x.size(0)
+        slots = self.top_k + 1
+        weights, ids = self._ops.route_topk(logits, self.top_k, self.norm_topk_prob,
+                                            shared_logits=self.shared_expert_gate(x))
+        flat_w = weights.view(-1)
+        # One EP rank: every expert is local and in order.
+        packed = self._ops.pack_routes(
+            ids.view(-1), flat_w, self.num_experts + 1, self.num_local_experts + 1,
+            expert_start=0, capacity=self._capacity(num_tokens), stats=stats,
+            num_shared_experts=1)
+        y = self._run_experts(x, flat_w, packed, slots, weights=self._shared_store())
+        self.total_assignment_count += num_tokens * self.top_k
+        return self._combine_expert_routes(y, packed.combine_rows, num_tokens, slots)
+
     def forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
         original_shape = hidden_states.shape
         x = hidden_states.reshape(-1, self.hidden_size)
+        fused_shared = self._fused_shared(x)
         if self.dispatch_backend in ("allgather_reduce", "allgather_reducescatter") \
                 and self.ep_size > 1:
             output = self._forward_global_dp(
@@ -624,7 +756,7 @@ class ExpertParallelMoE(nn.Module):
             from .ep import forward_rank0_all_to_all
             output = forward_rank0_all_to_all(self, x, self.dispatch_backend == "all_to_all_reduce")
         else:
-            output = self._forward_local(x)
+            output = self._forward_local(x, shared=fused_shared)
             if self.ep_size > 1:
                 group = dist_env.get_moe_group()
                 if self.fp64_staged_reduce:
@@ -638,7 +770,7 @@ class ExpertParallelMoE(nn.Module):
                     self.ep_all_reduce_count += 1
             elif output.dtype != x.dtype:
                 output = output.to(x.dtype)
-        if self.shared_expert is not None:
+        if self.shared_expert is not None and not fused_shared:
             shared = self.shared_expert(x)
             output = output + torch.sigmoid(self.shared_expert_gate(x)) * shared
         return output.reshape(original_shape)

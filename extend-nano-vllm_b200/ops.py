@@ -41,18 +41,32 @@ def _host_i32(values) -> ctypes.c_void_p:
     return ctypes.cast(arr, ctypes.c_void_p)
 
 
-def route_topk(logits: torch.Tensor, top_k: int, renormalize: bool
+def route_topk(logits: torch.Tensor, top_k: int, renormalize: bool,
+               shared_logits: torch.Tensor | None = None
                ) -> tuple[torch.Tensor, torch.Tensor]:
-    """fp32 softmax + top-k (+ renorm) of [T, E] logits -> (bf16 weights, int64 ids)."""
+    """fp32 softmax + top-k (+ renorm) of [T, E] logits -> (bf16 weights, int64 ids).
+
+    With ``shared_logits`` (bf16 [T] or [T, 1], the shared-expert gate's
+    output) the rows have top_k + 1 slots, the last one the shared expert
+    (id E, weight sigmoid of its gate logit)."""
     _require_cuda(logits)
     logits = logits.contiguous()
     if logits.dtype not in (torch.float32, torch.bfloat16, torch.float16):
         raise TypeError(f"router logits must be fp32/bf16/fp16, got {logits.dtype}")
     tokens, experts = logits.shape
-    weights = torch.empty((tokens, top_k), device=logits.device, dtype=torch.bfloat16)
-    ids = torch.empty((tokens, top_k), device=logits.device, dtype=torch.int64)
-    call("b200moe_route_topk", _p(logits), _DTYPE_CODES[logits.dtype], tokens, experts, top_k,
-         int(bool(renormalize)), _p(weights), _p(ids), _stream(logits))
+    slots = top_k if shared_logits is None else top_k + 1
+    weights = torch.empty((tokens, slots), device=logits.device, dtype=torch.bfloat16)
+    ids = torch.empty((tokens, slots), device=logits.device, dtype=torch.int64)
+    if shared_logits is None:
+        call("b200moe_route_topk", _p(logits), _DTYPE_CODES[logits.dtype], tokens, experts,
+             top_k, int(bool(renormalize)), _p(weights), _p(ids), _stream(logits))
+    else:
+        if shared_logits.dtype != torch.bfloat16 or shared_logits.numel() != tokens:
+            raise TypeError("shared_logits must be bf16 with one logit per token")
+        shared_logits = shared_logits.contiguous()
+        call("b200moe_route_topk_shared", _p(logits), _DTYPE_CODES[logits.dtype], tokens,
+             experts, top_k, int(bool(renormalize)), _p(shared_logits), _p(weights), _p(ids),
+             _stream(logits))
     return weights, ids
 
 
@@ -79,13 +93,16 @@ def pack_routes(expert_ids: torch.Tensor, route_weights: torch.Tensor | None,
                 local_index: torch.Tensor | None = None, expert_start: int = 0,
                 expert_base: torch.Tensor | None = None, capacity: int | None = None,
                 stats: torch.Tensor | None = None, route_count: torch.Tensor | None = None,
-                capacity_dev: torch.Tensor | None = None) -> PackedRoutes:
+                capacity_dev: torch.Tensor | None = None,
+                num_shared_experts: int = 0) -> PackedRoutes:
     """Capacity + expert-major packing of flat int64 routes.
 
     With ``capacity`` set, dropped routes are rewritten in place in
     ``expert_ids`` (to num_experts) and ``route_weights`` (to 0).
     ``route_count`` (device int32 [1]) packs only the first routes;
     ``capacity_dev`` (device int64 [1]) replaces ``capacity``.
+    ``num_shared_experts``: the last experts of ``num_experts`` are shared
+    experts (no capacity, not counted as kept routes).
     """
     _require_cuda(expert_ids)
     if expert_ids.dtype != torch.int64 or not expert_ids.is_contiguous():
@@ -115,7 +132,16 @@ def pack_routes(expert_ids: torch.Tensor, route_weights: torch.Tensor | None,
     if route_weights is not None and (route_weights.dtype != torch.bfloat16
                                       or route_weights.numel() != routes):
         raise TypeError("route_weights must be bf16 with one weight per route")
-    if route_count is None and capacity_dev is None:
+    if num_shared_experts:
+        if route_count is not None or capacity_dev is not None or expert_base is not None:
+            raise ValueError("shared experts are packed with host bounds only")
+        call("b200moe_pack_routes_shared", _p(flat), _p(route_weights), routes, num_experts,
+             int(num_shared_experts), _p(local_index), int(expert_start), num_local_experts,
+             -1 if capacity is None else int(capacity), row_capacity, _p(row_route),
+             _p(route_row), _p(combine_rows), _p(tile_expert), _p(expert_offsets),
+             _p(expert_counts), _p(mtiles), max_mtiles, _p(chunks), _p(counters), _p(stats),
+             _p(scratch), scratch.numel() * 4, _stream(flat))
+    elif route_count is None and capacity_dev is None:
         call("b200moe_pack_routes", _p(flat), _p(route_weights), routes, num_experts,
              _p(local_index), int(expert_start), num_local_experts, _p(expert_base),
              -1 if capacity is None else int(capacity), row_capacity, _p(row_route),

@@ -4,6 +4,8 @@ configurations (no datasets or checkpoints are used anywhere).
 Layer shapes:
   QWEN3_30B_A3B   hidden 2048, 128 experts, top-8, moe_intermediate 768
   QWEN3_235B_A22B hidden 4096, 128 experts, top-8, moe_intermediate 1536
+  QWEN3_NEXT_80B_A3B hidden 2048, 512 experts, top-10, moe_intermediate 512,
+                  shared expert 512
 Distributions: hidden states N(0, 1) bf16; router gate N(0, 0.02) fp32;
 expert weights N(0, 0.02) bf16; decode router logits U(0, 1) fp32; prefill
 logits N(0, 1) + Zipf(alpha) popularity bias over a seeded expert permutation.
@@ -30,6 +32,7 @@ class LayerShape:
     num_experts: int
     top_k: int
     norm_topk_prob: bool = True
+    shared_intermediate: int | None = None
 
     @property
     def expert_bytes(self) -> int:
@@ -44,6 +47,9 @@ class LayerShape:
 
 QWEN3_30B_A3B = LayerShape("qwen3-30b-a3b-moe", 2048, 768, 128, 8)
 QWEN3_235B_A22B = LayerShape("qwen3-235b-a22b-moe", 4096, 1536, 128, 8)
+# Qwen3-Next-style layer with a shared expert as wide as the routed ones.
+QWEN3_NEXT_80B_A3B = LayerShape("qwen3-next-80b-a3b-moe", 2048, 512, 512, 10,
+                                shared_intermediate=512)
 
 
 def _gen(seed: int) -> torch.Generator:
@@ -85,6 +91,17 @@ def expert_weights(shape: LayerShape, seed: int, num_local: int | None = None,
             w13[i] = (torch.randn((2 * I, H), generator=g) * 0.02).bfloat16()
             w2[i] = (torch.randn((H, I), generator=g) * 0.02).bfloat16()
     return w13, w2
+
+
+def shared_expert_weights(shape: LayerShape, seed: int, device="cpu"
+                          ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Shared expert (gate/up [2I_s, H], down [H, I_s], gate [1, H]) bf16, N(0, 0.02)."""
+    H, I = shape.hidden, shape.shared_intermediate
+    g = _gen(seed * 100003 + 99991)
+    w13 = (torch.randn((2 * I, H), generator=g) * 0.02).bfloat16()
+    w2 = (torch.randn((H, I), generator=g) * 0.02).bfloat16()
+    wg = (torch.randn((1, H), generator=g) * 0.02).bfloat16()
+    return w13.to(device), w2.to(device), wg.to(device)
 
 
 def uniform_logits(tokens: int, num_experts: int, seed: int, device="cpu") -> torch.Tensor:

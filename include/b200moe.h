@@ -106,6 +106,26 @@ B200MOE_API int b200moe_route_topk(const void *logits, int logits_dtype, int64_t
                        int num_experts, int top_k, int renormalize,
                        void *weights, int64_t *expert_ids, void *stream);
 
+/*
+ * b200moe_route_topk plus one shared-expert slot per token, for layers with a
+ * shared expert (moe.py:195-234, added at moe.py:1259-1262 as
+ * output + sigmoid(shared_expert_gate(x)) * shared_expert(x)).  Each output
+ * row holds top_k + 1 slots: the routed experts exactly as
+ * b200moe_route_topk writes them, then id num_experts with weight
+ * bf16(sigmoid(shared_logits[t])) (fp32 sigmoid of the bf16 gate logit, as
+ * torch.sigmoid on a bf16 tensor).  The shared expert then runs as expert
+ * num_experts of the grouped GEMMs (b200moe_pack_routes_shared), and the
+ * route-order combine adds it after the routed slots.
+ *   shared_logits [num_tokens] bf16 (the shared-expert gate's output)
+ *   weights       [num_tokens, top_k + 1] bf16 out
+ *   expert_ids    [num_tokens, top_k + 1] int64 out
+ * Limits: num_experts <= 1024, top_k <= min(31, num_experts).
+ */
+B200MOE_API int b200moe_route_topk_shared(const void *logits, int logits_dtype,
+                                          int64_t num_tokens, int num_experts, int top_k,
+                                          int renormalize, const void *shared_logits,
+                                          void *weights, int64_t *expert_ids, void *stream);
+
 /* Scratch bytes b200moe_pack_routes needs for `num_routes` routes. */
 B200MOE_API size_t b200moe_pack_scratch_bytes(int64_t num_routes, int num_experts);
 
@@ -181,6 +201,25 @@ B200MOE_API int b200moe_pack_routes_device_bounds(
     int32_t *tile_expert, int32_t *expert_offsets, int32_t *expert_counts, int32_t *mtiles,
     int64_t max_mtiles, int32_t *chunks, int32_t *counters, int64_t *stats, void *scratch,
     size_t scratch_bytes, void *stream);
+
+/*
+ * b200moe_pack_routes over routed plus shared experts: experts
+ * [num_experts - num_shared_experts, num_experts) are shared experts (routes
+ * written by b200moe_route_topk_shared); they have no capacity limit (the
+ * reference applies capacity to routed experts only, moe.py:879-919) and are
+ * left out of counters[B200MOE_CNT_LOCAL_KEPT] and `stats`.  Capacity
+ * positions and drops of the routed experts are those of b200moe_pack_routes
+ * over the routed slots alone (the shared slots form their own expert group).
+ * Dropped routes are rewritten to id = num_experts (routed + shared).
+ * Other arguments as b200moe_pack_routes without expert_base.
+ */
+B200MOE_API int b200moe_pack_routes_shared(
+    int64_t *expert_ids, void *route_weights, int64_t num_routes, int num_experts,
+    int num_shared_experts, const int64_t *local_index, int expert_start, int num_local_experts,
+    int64_t capacity, int64_t row_capacity, int32_t *row_route, int32_t *route_row,
+    int32_t *combine_rows, int32_t *tile_expert, int32_t *expert_offsets, int32_t *expert_counts,
+    int32_t *mtiles, int64_t max_mtiles, int32_t *chunks, int32_t *counters, int64_t *stats,
+    void *scratch, size_t scratch_bytes, void *stream);
 
 /*
  * b200moe_pack_routes for callers that cannot provide scratch memory.  No

@@ -126,3 +126,42 @@ def test_route_and_execute_local_seams():
     out, local = layer._execute_local(x, w, ids)
     assert local == int((ids < 8).sum())
     assert math.isfinite(float(out.float().abs().sum()))
+
+
+def test_shared_expert_weights_live_behind_the_routed_experts():
+    """A shared expert of the routed width is stored as expert E_loc of the
+    grouped storage; its parameters stay the reference's names, shapes and
+    loaders, and the storage survives dtype moves and state_dict loads."""
+    layer = ExpertParallelMoE(16, 32, 8, 2, True, shared_expert_intermediate_size=32)
+    shapes = {k: tuple(v.shape) for k, v in layer.state_dict().items()}
+    assert shapes == {"gate.weight": (8, 16), "gate_up_proj": (8, 64, 16),
+                      "down_proj": (8, 16, 32),
+                      "shared_expert.gate_up_proj.weight": (64, 16),
+                      "shared_expert.down_proj.weight": (16, 32),
+                      "shared_expert_gate.weight": (1, 16)}
+    shared = layer.shared_expert
+    with torch.no_grad():
+        for p in layer.parameters():
+            p.normal_(0, 0.02)
+    for dtype in (torch.float32, torch.bfloat16):
+        layer = layer.to(dtype)
+        w13, w2 = layer._shared_store()
+        assert w13.shape == (9, 64, 16) and w2.shape == (9, 16, 32)
+        assert w13.data_ptr() == layer.gate_up_proj.data_ptr()
+        assert w13[8].data_ptr() == shared.gate_up_proj.weight.data_ptr()
+        assert w2[8].data_ptr() == shared.down_proj.weight.data_ptr()
+    gate = torch.randn(32, 16).to(torch.bfloat16)
+    up = torch.randn(32, 16).to(torch.bfloat16)
+    loader = shared.gate_up_proj.weight.weight_loader
+    loader(shared.gate_up_proj.weight, gate, 0)
+    loader(shared.gate_up_proj.weight, up, 1)
+    w13, _ = layer._shared_store()
+    assert torch.equal(w13[8, :32], gate) and torch.equal(w13[8, 32:], up)
+    other = ExpertParallelMoE(16, 32, 8, 2, True,
+                              shared_expert_intermediate_size=32).to(torch.bfloat16)
+    other.load_state_dict(layer.state_dict())
+    o13, o2 = other._shared_store()
+    assert torch.equal(o13, w13) and torch.equal(o2[8], layer.shared_expert.down_proj.weight)
+    # A wider shared expert keeps its own storage (it runs after the routed output).
+    wide = ExpertParallelMoE(16, 32, 8, 2, True, shared_expert_intermediate_size=64)
+    assert not wide._shared_in_store
