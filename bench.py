@@ -28,6 +28,14 @@ nanovllm/layers/moe.py:546-580, restated in oracle/) on a bounded sample.
 At N = 1 the line also carries ``reference_triton_gpu``: the unmodified
 reference's own GPU path (Triton kernels, installed in baseline/_ref) timed
 on the same GPU with the same workloads and timing, and the speed-ups over it.
+At N > 1 it carries ``reference_ep_gpu``: the reference's all-gather +
+reduce-scatter backend on the same ranks and headline workload, and one
+CUDA-graph decode replay of the 30B-A3B layer at 8 and 32 tokens per rank,
+the reference's all-gather + all-reduce against this library's NVLink
+exchange.
+
+``--e2e b200|reference`` runs end-to-end offline generation through the
+reference's own engine instead (see e2e()).
 
 ``--impl reference`` times that CPU implementation alone on the host cores
 (rank 0 only) on the same workload and prints the same line with
@@ -93,7 +101,8 @@ def parse_args():
     p.add_argument("--no-sweep", action="store_true", help="skip the N=1 decode/prefill sweep")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-reference-triton", action="store_true",
-                   help="skip timing the reference's own GPU path (baseline/_ref) at N=1")
+                   help="skip timing the reference's own GPU path (baseline/_ref): its Triton "
+                        "path at N=1, its expert-parallel backends at N>1")
     p.add_argument("--profile-case", choices=("gemm-small", "decode", "prefill"), default=None,
                    help="run a case for ncu captures and exit (no JSON line): gemm-small = "
                         "235B-shaped experts, 16 experts x 320 routed rows, 604 MB of "
@@ -104,6 +113,15 @@ def parse_args():
     p.add_argument("--engine", default="auto",
                    choices=("auto", "tcgen05", "tcgen05-wide", "tcgen05-tall", "tcgen05-pair"),
                    help="expert GEMM engine of the headline layer (default: the library's choice)")
+    p.add_argument("--e2e", choices=("b200", "reference"), default=None,
+                   help="end-to-end offline generation through the reference's own engine "
+                        "(baseline/_ref) with DP x EP = --gpus replicas, its MoE layer "
+                        "('reference', all-gather backend) or this one ('b200', NVLink "
+                        "exchange); prints one JSON line of decode tokens/s")
+    p.add_argument("--e2e-requests", type=int, default=256)
+    p.add_argument("--e2e-prompt", type=int, default=1024)
+    p.add_argument("--e2e-output", type=int, default=256)
+    p.add_argument("--e2e-layers", type=int, default=48)
     p.add_argument("--profile-tokens", type=int, default=1)
     p.add_argument("--profile-engine", default="auto",
                    choices=("auto", "tcgen05-wide", "tcgen05-swap", "tcgen05-pair",
@@ -740,6 +758,115 @@ def reference_triton(steps: int, warmup: int) -> dict:
     return out
 
 
+# Decode batch sizes per rank of the expert-parallel latency comparison.
+EP_DECODE_TOKENS = (8, 32)
+
+
+def ep_graph_ms(forward, steps: int, warmup: int, world: int, flush, flush_read) -> float:
+    """Median device time of one CUDA-graph replay of ``forward()`` on every
+    rank at once (L2 flushed before each replay), max over ranks."""
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.no_grad(), torch.cuda.stream(stream):
+        for _ in range(3):
+            forward()
+    torch.cuda.current_stream().wait_stream(stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.no_grad(), torch.cuda.graph(graph):
+        forward()
+    for _ in range(warmup):
+        graph.replay()
+    barrier(world)
+    times = []
+    for _ in range(steps):
+        flush.fill_(1)
+        flush_read.amax()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        graph.replay()
+        b.record()
+        times.append((a, b))
+    torch.cuda.synchronize()
+    barrier(world)
+    del graph
+    return max_over_ranks(statistics.median(a.elapsed_time(b) for a, b in times), world)
+
+
+def reference_ep(args, world: int, rank: int, local: int) -> dict:
+    """The unmodified reference's expert-parallel backends on the same ranks
+    (baseline/_ref, its process groups from initialize_model_parallel):
+    all-gather + reduce-scatter at the headline workload, and decode latency
+    of one CUDA-graph replay at EP_DECODE_TOKENS tokens per rank on the
+    30B-A3B layer against this library's NVLink exchange (same weights)."""
+    import importlib
+
+    import extend_nano_vllm_b200.workloads as wl
+
+    ref_dir = os.path.join(REPO, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_dir, "nanovllm")):
+        return {"unavailable": "reference not installed in baseline/_ref"}
+    if ref_dir not in sys.path:
+        sys.path.append(ref_dir)
+    try:
+        ref_moe = importlib.import_module("nanovllm.layers.moe")
+        ps = importlib.import_module("nanovllm.distributed.parallel_state")
+    except Exception as exc:  # noqa: BLE001 - reported in the JSON line
+        return {"unavailable": f"reference import failed: {exc!r}"[:300]}
+    ps.initialize_model_parallel(1, 1, True, data_parallel_size=world)
+    device = torch.device("cuda", local)
+
+    def make_ref(shape, backend, **kw):
+        layer = ref_moe.ExpertParallelMoE(shape.hidden, shape.intermediate, shape.num_experts,
+                                          shape.top_k, shape.norm_topk_prob, ep_rank=rank,
+                                          ep_size=world, dispatch_backend=backend, **kw)
+        layer = layer.to(device=device, dtype=torch.bfloat16)
+        n = shape.num_experts // world
+        w13, w2 = wl.expert_weights(shape, seed=2024, num_local=n, first_expert=rank * n,
+                                    device=device, on_device=True)
+        with torch.no_grad():
+            layer.gate.weight.copy_(wl.gate_weight(shape, seed=2025).to(device))
+            layer.gate_up_proj.copy_(w13)
+            layer.down_proj.copy_(w2)
+        return layer
+
+    out = {}
+    shape = wl.QWEN3_235B_A22B
+    layer = make_ref(shape, "allgather_reducescatter")
+    x = wl.hidden_states(TOKENS_PER_GPU, shape.hidden, seed=1000 + rank, device=device)
+    steps = max(5, args.steps // 4)
+    with torch.no_grad():
+        seconds = time_steps(lambda: layer(x), steps, min(3, args.warmup), world)
+    ms = seconds / steps * 1e3
+    out["headline_allgather_reducescatter"] = {
+        "ms": round(ms, 4), "tokens_per_s": round(world * TOKENS_PER_GPU / (ms / 1e3), 1)}
+    del layer, x
+    torch.cuda.empty_cache()
+
+    shape = wl.QWEN3_30B_A3B
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    flush_read = torch.ones(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    ref_layer = make_ref(shape, "allgather_reduce", graph_safe_decode=True)
+    own_layer = build_layer(shape, world, rank, device, graph_safe_decode=True)
+    decode = []
+    for tokens in EP_DECODE_TOKENS:
+        x = wl.hidden_states(tokens, shape.hidden, seed=300 + tokens + 17 * rank, device=device)
+        row = {"tokens_per_rank": tokens}
+        row["reference_allgather_reduce_us"] = round(1e3 * ep_graph_ms(
+            lambda: ref_layer(x), max(20, args.steps // 4), args.warmup, world, flush,
+            flush_read), 2)
+        row["nvlink_exchange_us"] = round(1e3 * ep_graph_ms(
+            lambda: own_layer(x), max(20, args.steps // 4), args.warmup, world, flush,
+            flush_read), 2)
+        row["speedup"] = round(row["reference_allgather_reduce_us"]
+                               / row["nvlink_exchange_us"], 2)
+        decode.append(row)
+    out["decode_30b_a3b_graph"] = decode
+    del ref_layer, own_layer, flush, flush_read
+    torch.cuda.empty_cache()
+    return out
+
+
 def native(args, world, rank, local, json_fd: int = 1) -> None:
     import extend_nano_vllm_b200 as pkg
     import extend_nano_vllm_b200.workloads as wl
@@ -859,6 +986,12 @@ def native(args, world, rank, local, json_fd: int = 1) -> None:
                         str(r["tokens"]): round(r["ms"] / n["ms_fused"], 2)
                         for r, n in zip(ref.get("shared_next_decode", []),
                                         sweep["shared_expert_next"]["buckets"])}}
+    if world > 1 and not args.no_reference_triton:
+        ref = reference_ep(args, world, rank, local)
+        record["reference_ep_gpu"] = ref
+        if "headline_allgather_reducescatter" in ref:
+            record["speedup_vs_reference_ep_gpu"] = round(
+                ref["headline_allgather_reducescatter"]["ms"] / ms_per_step, 2)
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         record["cpu_baseline"] = cpu_config1_baseline(wl)
     if rank == 0:
@@ -915,8 +1048,236 @@ def reference(args, world, rank) -> None:
     print(json.dumps(record), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# End-to-end offline generation (the benchmark list's last configuration):
+# the reference's unchanged engine (LLM, scheduler, model runner with paged KV
+# cache and decode CUDA graphs, data-parallel replicas sharing one MoE group)
+# on a random-init Qwen3-30B-A3B-architecture model, with the reference's MoE
+# layer or this one swapped in at import time, the way the integration patch
+# at the end of nanovllm/layers/moe.py would.
+# ---------------------------------------------------------------------------
+E2E_MODEL = dict(hidden_size=2048, num_attention_heads=32, num_key_value_heads=4, head_dim=128,
+                 num_experts=128, num_experts_per_tok=8, moe_intermediate_size=768,
+                 intermediate_size=6144, vocab_size=151936, norm_topk_prob=True,
+                 max_position_embeddings=40960, rope_theta=1000000.0, rms_norm_eps=1e-6,
+                 tie_word_embeddings=False, decoder_sparse_step=1, mlp_only_layers=[],
+                 bos_token_id=151643, eos_token_id=151645)
+E2E_SEED = 20251
+
+
+def e2e_model_dir(root: str, layers: int) -> str:
+    """Config-only checkpoint directory (no weights) plus a word-level
+    tokenizer over the model's vocabulary ("t<id>"): prompts are token ids and
+    generation ignores EOS, so the tokenizer only names the EOS id and turns
+    the outputs back into text."""
+    from tokenizers import Tokenizer, models, pre_tokenizers
+    from transformers import PreTrainedTokenizerFast, Qwen3MoeConfig
+
+    config = Qwen3MoeConfig(**{**E2E_MODEL, "num_hidden_layers": layers}, dtype="bfloat16")
+    config.save_pretrained(root)
+    vocab = {f"t{i}": i for i in range(E2E_MODEL["vocab_size"])}
+    tok = Tokenizer(models.WordLevel(vocab=vocab, unk_token="t0"))
+    tok.pre_tokenizer = pre_tokenizers.WhitespaceSplit()
+    PreTrainedTokenizerFast(tokenizer_object=tok, unk_token="t0",
+                            eos_token=f"t{E2E_MODEL['eos_token_id']}").save_pretrained(root)
+    return root
+
+
+def e2e_random_init(model, path) -> None:
+    """Stands in for nanovllm.utils.loader.load_model (no checkpoint exists):
+    every parameter N(0, 0.02) from a generator seeded by its name, norms 1.
+    Both arms name and shard their parameters alike, so they get the same
+    weights."""
+    import zlib
+
+    with torch.no_grad():
+        for name, param in model.named_parameters():
+            if "norm" in name:
+                param.fill_(1.0)
+                continue
+            g = torch.Generator(device=param.device)
+            g.manual_seed(E2E_SEED * 1000003 + zlib.crc32(name.encode()))
+            param.normal_(0.0, 0.02, generator=g)
+
+
+def e2e_install_b200_layer() -> None:
+    """Make every nanovllm module that imported the reference's
+    ExpertParallelMoE use this repository's class; the engine's cross-DP
+    all-gather backend becomes the NVLink exchange."""
+    import nanovllm.layers.moe as ref_moe
+
+    from extend_nano_vllm_b200.moe import ExpertParallelMoE as B200MoE
+
+    class EngineMoE(B200MoE):
+        def __init__(self, *args, dispatch_backend: str = "replicated", **kwargs):
+            if dispatch_backend in ("allgather_reduce", "allgather_reducescatter"):
+                dispatch_backend = "all_to_all_nvlink"
+            super().__init__(*args, dispatch_backend=dispatch_backend, **kwargs)
+
+    original = ref_moe.ExpertParallelMoE
+    for module in list(sys.modules.values()):
+        if (getattr(module, "__name__", "").startswith("nanovllm")
+                and getattr(module, "ExpertParallelMoE", None) is original):
+            module.ExpertParallelMoE = EngineMoE
+
+
+def e2e_replica(replica_id, dp, model_dir, indexed_prompts, max_tokens, queue, kwargs, impl):
+    """One data-parallel replica (the reference's data_parallel._run_replica,
+    plus step timing): its own LLM engine on GPU `replica_id`."""
+    import traceback
+
+    llm = None
+    try:
+        ref_dir = os.path.join(REPO, "baseline", "_ref")
+        if ref_dir not in sys.path:
+            sys.path.insert(0, ref_dir)
+        import nanovllm.engine.model_runner as runner_mod
+        import nanovllm.utils.loader as loader_mod
+        from nanovllm import LLM, SamplingParams
+        from nanovllm.engine.llm_engine import LLMEngine
+
+        loader_mod.load_model = e2e_random_init
+        runner_mod.load_model = e2e_random_init
+        if impl == "b200":
+            e2e_install_b200_layer()
+        stats = {"prefill_s": 0.0, "prefill_tokens": 0, "decode_s": 0.0, "decode_tokens": 0,
+                 "decode_steps": 0}
+        step = LLMEngine.step
+        step_ms = []
+        prefill_ms = []
+
+        def timed_step(self):
+            t0 = time.perf_counter()
+            outputs, num_tokens = step(self)
+            dt = time.perf_counter() - t0
+            if num_tokens > 0:
+                stats["prefill_s"] += dt
+                stats["prefill_tokens"] += num_tokens
+                prefill_ms.append(round(dt * 1e3, 2))
+            elif num_tokens < 0:
+                stats["decode_s"] += dt
+                stats["decode_tokens"] += -num_tokens
+                stats["decode_steps"] += 1
+                step_ms.append(dt * 1e3)
+            return outputs, num_tokens
+
+        LLMEngine.step = timed_step
+        t0 = time.perf_counter()
+        llm = LLM(model_dir, data_parallel_size=dp, data_parallel_rank=replica_id, **kwargs)
+        stats["init_s"] = time.perf_counter() - t0
+        _, prompts = zip(*indexed_prompts)
+        params = SamplingParams(temperature=0.0, max_tokens=max_tokens, ignore_eos=True)
+        t0 = time.perf_counter()
+        outputs = llm.generate(list(prompts), params, use_tqdm=False)
+        stats["generate_s"] = time.perf_counter() - t0
+        stats["output_tokens"] = sum(len(o["token_ids"]) for o in outputs)
+        stats["first_tokens"] = [o["token_ids"][:8] for o in outputs[:2]]
+        stats["decode_step_ms_median"] = statistics.median(step_ms) if step_ms else None
+        stats["decode_step_ms_first"] = [round(v, 2) for v in step_ms[:3]]
+        stats["prefill_step_ms"] = prefill_ms
+        stats["decode_graph_replays"] = getattr(llm.model_runner, "decode_graph_replay_count",
+                                                None)
+        queue.put((replica_id, stats, None))
+    except Exception:  # noqa: BLE001 - reported to the parent
+        queue.put((replica_id, None, traceback.format_exc()))
+    finally:
+        if llm is not None:
+            llm.exit()
+
+
+def e2e(args) -> None:
+    """DP x EP = --gpus replicas of the reference engine (generate_data_parallel's
+    launch: one spawned process per replica, a shared MoE group over all of
+    them, prompts dealt round-robin, equal max_tokens, EOS ignored)."""
+    import multiprocessing as mp
+    import socket
+    import tempfile
+    from queue import Empty
+
+    dp = args.gpus
+    gen = torch.Generator().manual_seed(E2E_SEED)
+    prompts = torch.randint(0, E2E_MODEL["vocab_size"], (args.e2e_requests, args.e2e_prompt),
+                            generator=gen).tolist()
+    with socket.socket() as sock:
+        sock.bind(("127.0.0.1", 0))
+        port = sock.getsockname()[1]
+    per_rank = args.e2e_requests // dp
+    kwargs = dict(enable_expert_parallel=dp > 1, master_port=port, max_num_seqs=per_rank,
+                  max_model_len=2048, max_num_batched_tokens=8192)
+    assignments = [[] for _ in range(dp)]
+    for index, prompt in enumerate(prompts):
+        assignments[index % dp].append((index, prompt))
+    root = tempfile.mkdtemp(prefix="e2e_model_")
+    e2e_model_dir(root, args.e2e_layers)
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    procs = [ctx.Process(target=e2e_replica, args=(r, dp, root, assignments[r], args.e2e_output,
+                                                    queue, kwargs, args.e2e))
+             for r in range(dp)]
+    t0 = time.perf_counter()
+    for p in procs:
+        p.start()
+    results, errors = {}, []
+    for _ in procs:
+        try:
+            rid, stats, err = queue.get(timeout=900)
+        except Empty:
+            errors.append("timed out waiting for a replica")
+            break
+        if err:
+            errors.append(f"replica {rid}: {err}")
+        else:
+            results[rid] = stats
+    wall = time.perf_counter() - t0
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.terminate()
+            p.join()
+    record = {"metric": "e2e decode tokens/s (offline generation, DP x EP)", "impl": args.e2e,
+              "n_gpus": dp, "unit": "tokens/s", "higher_is_better": True,
+              "data": "random-init weights, seeded uniform prompt token ids",
+              "config": {"model": f"Qwen3-30B-A3B architecture, {args.e2e_layers} layers",
+                         "requests": args.e2e_requests, "prompt_tokens": args.e2e_prompt,
+                         "output_tokens": args.e2e_output, "parallelism": f"dp{dp}xep{dp}",
+                         "moe_backend": ("all_to_all_nvlink (this repository)"
+                                         if args.e2e == "b200" else
+                                         "allgather_reduce (reference)"),
+                         "kvcache_block_size": 256, "decode_cuda_graphs": True},
+              "wall_s": round(wall, 1)}
+    if errors or len(results) != dp:
+        record["error"] = "\n".join(errors)[-4000:]
+    else:
+        decode_s = max(r["decode_s"] for r in results.values())
+        prefill_s = max(r["prefill_s"] for r in results.values())
+        decode_tokens = sum(r["decode_tokens"] for r in results.values())
+        prefill_tokens = sum(r["prefill_tokens"] for r in results.values())
+        generate_s = max(r["generate_s"] for r in results.values())
+        record.update({
+            "value": round(decode_tokens / decode_s, 1),
+            "decode_s": round(decode_s, 3), "decode_tokens": decode_tokens,
+            "decode_steps": max(r["decode_steps"] for r in results.values()),
+            "prefill_tokens_per_s": round(prefill_tokens / prefill_s, 1),
+            "generate_s": round(generate_s, 3),
+            "output_tokens_per_s": round(sum(r["output_tokens"] for r in results.values())
+                                         / generate_s, 1),
+            "init_s": round(max(r["init_s"] for r in results.values()), 1),
+            "decode_step_ms_median": [round(r["decode_step_ms_median"], 3)
+                                      for _, r in sorted(results.items())],
+            "decode_step_ms_first": results[0]["decode_step_ms_first"],
+            "prefill_step_ms": results[0]["prefill_step_ms"],
+            "decode_graph_replays": [r["decode_graph_replays"] for _, r in sorted(results.items())],
+            "first_tokens": results[0]["first_tokens"]})
+    print(json.dumps(record), flush=True)
+    if "error" in record:
+        sys.exit(1)
+
+
 def main() -> None:
     args = parse_args()
+    if args.e2e:
+        e2e(args)
+        return
     if args.profile_case:
         profile_case(args)
         return

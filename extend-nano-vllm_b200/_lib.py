@@ -49,6 +49,8 @@ SIGNATURES: dict[str, tuple] = {
                                  _P, _P, _L, _P, _P, _P, _P, _S, _P]),
     "b200moe_pack_routes_shared": (_I, [_P, _P, _L, _I, _I, _P, _I, _I, _L, _L, _P, _P, _P, _P,
                                         _P, _P, _P, _L, _P, _P, _P, _P, _S, _P]),
+    "b200moe_route_pack": (_I, [_P, _I, _L, _I, _I, _I, _P, _P, _P, _I, _I, _L, _L, _P, _P, _P,
+                                _P, _P, _P, _P, _L, _P, _P, _P, _P, _S, _P]),
     "b200moe_pack_static_scratch_capacity": (_S, []),
     "b200moe_pack_routes_static_scratch": (_I, [_P, _P, _L, _I, _P, _I, _I, _P, _L, _L, _P, _P,
                                                 _P, _P, _P, _P, _P, _L, _P, _P, _P]),

@@ -20,6 +20,7 @@
 // With a single route block (up to 1024 routes: decode buckets) pack_scatter
 // does pack_hist's work itself and pack_hist is not launched.
 #include "common.cuh"
+#include "route_warp.cuh"
 
 namespace b200moe {
 namespace {
@@ -125,9 +126,40 @@ struct ScatterArgs {
 // Shared memory (int32 words): base[E1] tot[E1] run[E1] loc[E1]
 // warp_cnt[8][E1] lstart[L] lkept[L] gof[L] mstart[L] cstart[L] + 5 reduction
 // words.
+__device__ __forceinline__ void pack_scatter_body(const ScatterArgs &a);
+
 __global__ void __launch_bounds__(kPackThreads) pack_scatter_kernel(ScatterArgs a) {
   pdl_trigger();
   pdl_wait();
+  pack_scatter_body(a);
+}
+
+// Small batches (one route block): the router and the packing in one launch.
+// Warp w routes tokens w, w + 8, ... exactly as route_topk_kernel does (same
+// warp routine), writes ids and bf16 weights, and after a block barrier the
+// block packs them (the single-block pack_scatter work).
+template <typename T, int VPL>
+__global__ void __launch_bounds__(kPackThreads) route_pack_kernel(
+    const T *logits, int64_t num_tokens, int top_k, int renormalize, ScatterArgs a) {
+  pdl_trigger();
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  for (int64_t t = warp; t < num_tokens; t += kPackWarps) {
+    float w;
+    int id;
+    warp_route_token<T, VPL>(logits + t * a.num_experts, a.num_experts, top_k, renormalize,
+                             lane, &w, &id);
+    if (lane < top_k) {
+      a.weights[t * top_k + lane] = __float2bfloat16_rn(w);
+      a.ids[t * top_k + lane] = id;
+    }
+  }
+  __syncthreads();
+  pack_scatter_body(a);
+}
+
+__device__ __forceinline__ void pack_scatter_body(const ScatterArgs &a) {
   extern __shared__ int32_t sm[];
   const int E = a.num_experts;
   const int E1 = E + 1;
@@ -394,6 +426,41 @@ __global__ void histogram_kernel(const int64_t *__restrict__ ids, int64_t num_ro
     if (sh[e]) atomicAdd(&counts[e], sh[e]);
 }
 
+// Routing done inside the packing launch (b200moe_route_pack).
+struct RouteSpec {
+  const void *logits;
+  int dtype;
+  int64_t tokens;
+  int top_k;
+  int renormalize;
+};
+
+template <typename T>
+int launch_route_pack(const RouteSpec &r, const ScatterArgs &a, size_t smem, cudaStream_t s) {
+  const int vpl = (a.num_experts + 31) / 32;
+  const T *lg = static_cast<const T *>(r.logits);
+#define B200_ROUTE_PACK_CASE(V)                                                             \
+  if (vpl <= V) {                                                                           \
+    if (smem > 48 * 1024)                                                                   \
+      B200_CUDA(cudaFuncSetAttribute(route_pack_kernel<T, V>,                               \
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,           \
+                                     static_cast<int>(smem)));                              \
+    B200_LAUNCH_PDL(kPdlPack, route_pack_kernel<T, V>, dim3(1), dim3(kPackThreads), smem, s, \
+                    lg, r.tokens, r.top_k, r.renormalize, a);                               \
+    B200_LAUNCHED();                                                                        \
+    return B200MOE_OK;                                                                      \
+  }
+  B200_ROUTE_PACK_CASE(1)
+  B200_ROUTE_PACK_CASE(2)
+  B200_ROUTE_PACK_CASE(4)
+  B200_ROUTE_PACK_CASE(8)
+  B200_ROUTE_PACK_CASE(16)
+  B200_ROUTE_PACK_CASE(32)
+#undef B200_ROUTE_PACK_CASE
+  set_error("num_experts %d exceeds 1024", a.num_experts);
+  return B200MOE_EUNSUPPORTED;
+}
+
 size_t scatter_smem_bytes(int num_experts, int num_local) {
   const size_t E1 = static_cast<size_t>(num_experts) + 1;
   return sizeof(int32_t) * (E1 * (4 + kPackWarps) + 5 * static_cast<size_t>(num_local) + 5);
@@ -411,7 +478,8 @@ static int pack_routes_impl(int64_t *expert_ids, void *route_weights, int64_t nu
                             int32_t *combine_rows, int32_t *tile_expert, int32_t *expert_offsets,
                             int32_t *expert_counts, int32_t *mtiles, int64_t max_mtiles,
                             int32_t *chunks, int32_t *counters, int64_t *stats, void *scratch,
-                            size_t scratch_bytes, void *stream) {
+                            size_t scratch_bytes, void *stream,
+                            const b200moe::RouteSpec *route = nullptr) {
   using namespace b200moe;
   B200_ARG(num_routes >= 0 && num_routes < (int64_t)0x7fffffff, "num_routes out of range");
   B200_ARG(num_experts >= 1 && num_experts <= 4096, "num_experts must be in [1, 4096]");
@@ -477,6 +545,20 @@ static int pack_routes_impl(int64_t *expert_ids, void *route_weights, int64_t nu
   a.nblk = g.nblk;
   a.single = single ? 1 : 0;
   const size_t smem = scatter_smem_bytes(num_experts, num_local_experts);
+  if (route != nullptr) {
+    B200_ARG(single && route->tokens * route->top_k == num_routes,
+             "routing inside the packing launch needs num_tokens * top_k = num_routes <= %d",
+             B200MOE_ROUTE_PACK_MAX_ROUTES);
+    B200_ARG(route_weights != nullptr && route->logits != nullptr, "null pointer argument");
+    switch (route->dtype) {
+      case B200MOE_F32: return launch_route_pack<float>(*route, a, smem, s);
+      case B200MOE_BF16: return launch_route_pack<__nv_bfloat16>(*route, a, smem, s);
+      case B200MOE_F16: return launch_route_pack<__half>(*route, a, smem, s);
+      default:
+        set_error("unsupported logits dtype code %d", route->dtype);
+        return B200MOE_EINVAL;
+    }
+  }
   if (smem > 48 * 1024) {
     B200_CUDA(cudaFuncSetAttribute(pack_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    static_cast<int>(smem)));
@@ -549,6 +631,28 @@ int b200moe_pack_routes_shared(int64_t *expert_ids, void *route_weights, int64_t
                           route_row, combine_rows, tile_expert, expert_offsets, expert_counts,
                           mtiles, max_mtiles, chunks, counters, stats, scratch, scratch_bytes,
                           stream);
+}
+
+int b200moe_route_pack(const void *logits, int logits_dtype, int64_t num_tokens,
+                       int num_experts, int top_k, int renormalize, void *weights,
+                       int64_t *expert_ids, const int64_t *local_index, int expert_start,
+                       int num_local_experts, int64_t capacity, int64_t row_capacity,
+                       int32_t *row_route, int32_t *route_row, int32_t *combine_rows,
+                       int32_t *tile_expert, int32_t *expert_offsets, int32_t *expert_counts,
+                       int32_t *mtiles, int64_t max_mtiles, int32_t *chunks, int32_t *counters,
+                       int64_t *stats, void *scratch, size_t scratch_bytes, void *stream) {
+  B200_ARG(num_tokens >= 1, "num_tokens must be >= 1");
+  B200_ARG(top_k >= 1 && top_k <= num_experts, "top_k must be between 1 and num_experts");
+  B200_UNSUPPORTED(top_k <= 32, "top_k %d > 32 is not supported", top_k);
+  B200_UNSUPPORTED(num_experts <= 1024, "num_experts %d > 1024 is not supported", num_experts);
+  B200_ARG(num_tokens * top_k <= B200MOE_ROUTE_PACK_MAX_ROUTES,
+           "num_tokens * top_k must be <= %d", B200MOE_ROUTE_PACK_MAX_ROUTES);
+  const b200moe::RouteSpec route{logits, logits_dtype, num_tokens, top_k, renormalize};
+  return pack_routes_impl(expert_ids, weights, num_tokens * top_k, num_experts, 0, local_index,
+                          expert_start, num_local_experts, nullptr, capacity, nullptr, nullptr,
+                          row_capacity, row_route, route_row, combine_rows, tile_expert,
+                          expert_offsets, expert_counts, mtiles, max_mtiles, chunks, counters,
+                          stats, scratch, scratch_bytes, stream, &route);
 }
 
 int b200moe_expert_histogram(const int64_t *expert_ids, int64_t num_routes, int num_experts,

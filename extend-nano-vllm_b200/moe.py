@@ -53,6 +53,11 @@ GRAPH_SAFE_BACKENDS = ("replicated", "allgather_reduce", "allgather_reducescatte
                        "all_to_all_nvlink")
 
 
+# Batches of up to this many tokens route and pack in one launch (the packing
+# block's 8 warps route two tokens each at most).
+ROUTE_PACK_MAX_TOKENS = 16
+
+
 def _capturing() -> bool:
     return torch.cuda.is_available() and torch.cuda.is_current_stream_capturing()
 
@@ -706,10 +711,22 @@ class ExpertParallelMoE(nn.Module):
                 logits, x.contiguous(), self.gate_up_proj, self.down_proj, self.top_k,
                 self.norm_topk_prob, self.num_experts, local_index=local_index,
                 expert_start=max(self.expert_start, 0), stats=stats)
-        weights, ids = self._ops.route_topk(logits, self.top_k, self.norm_topk_prob)
+        if (self._ops is _native_ops and num_tokens <= ROUTE_PACK_MAX_TOKENS
+                and num_tokens * self.top_k <= _native_ops.ROUTE_PACK_MAX_ROUTES
+                and self.num_experts <= 1024 and self.top_k <= 32):
+            # Small batches: router and packing in one launch (same results).
+            local_index = (self.expert_local_index_tensor if self.expert_id_to_local is not None
+                           else None)
+            weights, ids, packed = self._ops.route_pack(
+                logits, self.top_k, self.norm_topk_prob, self.num_experts,
+                self.num_local_experts, local_index=local_index,
+                expert_start=max(self.expert_start, 0), capacity=self._capacity(num_tokens),
+                stats=stats)
+        else:
+            weights, ids = self._ops.route_topk(logits, self.top_k, self.norm_topk_prob)
+            packed = self._pack(ids.view(-1), weights.view(-1),
+                                capacity=self._capacity(num_tokens), stats=stats)
         flat_w = weights.view(-1)
-        packed = self._pack(ids.view(-1), flat_w, capacity=self._capacity(num_tokens),
-                            stats=stats)
         y = self._run_experts(x, flat_w, packed, self.top_k)
         self.total_assignment_count += ids.numel()
         return self._combine_expert_routes(y, packed.combine_rows, num_tokens, self.top_k)

@@ -88,6 +88,64 @@ class PackedRoutes:
     chunks: torch.Tensor | None = None  # [max_mtiles, 3] int32 row chunks of <= 256 rows
 
 
+def _layout_buffers(routes: int, num_experts: int, num_local_experts: int,
+                    device: torch.device):
+    row_capacity = int(_lib.LIB.b200moe_pack_row_capacity(routes, num_local_experts))
+    max_mtiles = int(_lib.LIB.b200moe_pack_max_mtiles(routes, num_local_experts))
+    scratch_bytes = int(_lib.LIB.b200moe_pack_scratch_bytes(routes, num_experts))
+    i32 = dict(device=device, dtype=torch.int32)
+    return (row_capacity, max_mtiles,
+            torch.empty(row_capacity, **i32),                                # row_route
+            torch.empty(routes, **i32),                                      # route_row
+            torch.empty(routes, **i32),                                      # combine_rows
+            torch.empty(row_capacity // _lib.BLOCK_ROWS, **i32),             # tile_expert
+            torch.empty(num_local_experts + 1, **i32),                       # expert_offsets
+            torch.empty(num_local_experts, **i32),                           # expert_counts
+            torch.empty((max(1, max_mtiles), _lib.MTILE_WORDS), **i32),      # mtiles
+            torch.empty((max(1, max_mtiles), _lib.MTILE_WORDS), **i32),      # chunks
+            torch.empty(_lib.NUM_COUNTERS, **i32),                           # counters
+            torch.empty(max(1, scratch_bytes // 4), **i32))                  # scratch
+
+
+# Largest route count b200moe_route_pack takes (one route block).
+ROUTE_PACK_MAX_ROUTES = 1024
+
+
+def route_pack(logits: torch.Tensor, top_k: int, renormalize: bool, num_experts: int,
+               num_local_experts: int, *, local_index: torch.Tensor | None = None,
+               expert_start: int = 0, capacity: int | None = None,
+               stats: torch.Tensor | None = None
+               ) -> tuple[torch.Tensor, torch.Tensor, "PackedRoutes"]:
+    """route_topk + pack_routes in one launch for <= ROUTE_PACK_MAX_ROUTES
+    routes -> (bf16 weights [T, k], int64 ids [T, k], packed layout)."""
+    _require_cuda(logits)
+    logits = logits.contiguous()
+    if logits.dtype not in (torch.float32, torch.bfloat16, torch.float16):
+        raise TypeError(f"router logits must be fp32/bf16/fp16, got {logits.dtype}")
+    tokens, experts = logits.shape
+    if experts != num_experts:
+        raise ValueError("logits must have one column per expert")
+    routes = tokens * top_k
+    device = logits.device
+    weights = torch.empty((tokens, top_k), device=device, dtype=torch.bfloat16)
+    ids = torch.empty((tokens, top_k), device=device, dtype=torch.int64)
+    (row_capacity, max_mtiles, row_route, route_row, combine_rows, tile_expert, expert_offsets,
+     expert_counts, mtiles, chunks, counters, scratch) = _layout_buffers(
+        routes, num_experts, num_local_experts, device)
+    if local_index is not None and (local_index.dtype != torch.int64
+                                    or local_index.numel() != num_experts):
+        raise TypeError("local_index must be int64 [num_experts]")
+    call("b200moe_route_pack", _p(logits), _DTYPE_CODES[logits.dtype], tokens, experts, top_k,
+         int(bool(renormalize)), _p(weights), _p(ids), _p(local_index), int(expert_start),
+         num_local_experts, -1 if capacity is None else int(capacity), row_capacity,
+         _p(row_route), _p(route_row), _p(combine_rows), _p(tile_expert), _p(expert_offsets),
+         _p(expert_counts), _p(mtiles), max_mtiles, _p(chunks), _p(counters), _p(stats),
+         _p(scratch), scratch.numel() * 4, _stream(logits))
+    return weights, ids, PackedRoutes(routes, row_capacity, max_mtiles, row_route, route_row,
+                                      combine_rows, tile_expert, expert_offsets, expert_counts,
+                                      mtiles, counters, chunks)
+
+
 def pack_routes(expert_ids: torch.Tensor, route_weights: torch.Tensor | None,
                 num_experts: int, num_local_experts: int, *,
                 local_index: torch.Tensor | None = None, expert_start: int = 0,
@@ -109,21 +167,9 @@ def pack_routes(expert_ids: torch.Tensor, route_weights: torch.Tensor | None,
         raise TypeError("expert_ids must be a contiguous int64 tensor")
     flat = expert_ids.view(-1)
     routes = flat.numel()
-    device = flat.device
-    row_capacity = int(_lib.LIB.b200moe_pack_row_capacity(routes, num_local_experts))
-    max_mtiles = int(_lib.LIB.b200moe_pack_max_mtiles(routes, num_local_experts))
-    scratch_bytes = int(_lib.LIB.b200moe_pack_scratch_bytes(routes, num_experts))
-    i32 = dict(device=device, dtype=torch.int32)
-    row_route = torch.empty(row_capacity, **i32)
-    route_row = torch.empty(routes, **i32)
-    combine_rows = torch.empty(routes, **i32)
-    tile_expert = torch.empty(row_capacity // _lib.BLOCK_ROWS, **i32)
-    expert_offsets = torch.empty(num_local_experts + 1, **i32)
-    expert_counts = torch.empty(num_local_experts, **i32)
-    mtiles = torch.empty((max(1, max_mtiles), _lib.MTILE_WORDS), **i32)
-    chunks = torch.empty((max(1, max_mtiles), _lib.MTILE_WORDS), **i32)
-    counters = torch.empty(_lib.NUM_COUNTERS, **i32)
-    scratch = torch.empty(max(1, scratch_bytes // 4), **i32)
+    (row_capacity, max_mtiles, row_route, route_row, combine_rows, tile_expert, expert_offsets,
+     expert_counts, mtiles, chunks, counters, scratch) = _layout_buffers(
+        routes, num_experts, num_local_experts, flat.device)
     if local_index is not None:
         if local_index.dtype != torch.int64 or local_index.numel() != num_experts:
             raise TypeError("local_index must be int64 [num_experts]")

@@ -203,6 +203,27 @@ B200MOE_API int b200moe_pack_routes_device_bounds(
     size_t scratch_bytes, void *stream);
 
 /*
+ * b200moe_route_topk followed by b200moe_pack_routes in one launch, for small
+ * batches (num_tokens * top_k <= B200MOE_ROUTE_PACK_MAX_ROUTES: one route
+ * block).  Writes the same weights/expert_ids as b200moe_route_topk (the same
+ * warp routine; capacity drops then applied in place as b200moe_pack_routes
+ * does) and the same layout as b200moe_pack_routes over them.  Replaces
+ * moe.py:870-919 plus the packing lines of b200moe_pack_routes.
+ *   weights    [num_tokens, top_k] bf16 out;  expert_ids [num_tokens, top_k] int64 out
+ * Other arguments as b200moe_pack_routes (num_routes = num_tokens * top_k,
+ * no expert_base).
+ */
+#define B200MOE_ROUTE_PACK_MAX_ROUTES 1024
+B200MOE_API int b200moe_route_pack(
+    const void *logits, int logits_dtype, int64_t num_tokens, int num_experts, int top_k,
+    int renormalize, void *weights, int64_t *expert_ids, const int64_t *local_index,
+    int expert_start, int num_local_experts, int64_t capacity, int64_t row_capacity,
+    int32_t *row_route, int32_t *route_row, int32_t *combine_rows, int32_t *tile_expert,
+    int32_t *expert_offsets, int32_t *expert_counts, int32_t *mtiles, int64_t max_mtiles,
+    int32_t *chunks, int32_t *counters, int64_t *stats, void *scratch, size_t scratch_bytes,
+    void *stream);
+
+/*
  * b200moe_pack_routes over routed plus shared experts: experts
  * [num_experts - num_shared_experts, num_experts) are shared experts (routes
  * written by b200moe_route_topk_shared); they have no capacity limit (the
