@@ -42,6 +42,7 @@ SIGNATURES: dict[str, tuple] = {
     "b200moe_device_status": (_I, [_P, _I]),
     "b200moe_route_topk": (_I, [_P, _I, _L, _I, _I, _I, _P, _P, _P]),
     "b200moe_route_topk_shared": (_I, [_P, _I, _L, _I, _I, _I, _P, _P, _P, _P]),
+    "b200moe_route_gate_topk": (_I, [_P, _I, _P, _L, _I, _I, _I, _P, _P, _P, _P, _P]),
     "b200moe_pack_scratch_bytes": (_S, [_L, _I]),
     "b200moe_pack_row_capacity": (_L, [_L, _I]),
     "b200moe_pack_max_mtiles": (_L, [_L, _I]),

@@ -255,6 +255,12 @@ class ExpertParallelMoE(nn.Module):
         # False: compute the shared expert after the routed output, as the
         # reference does, even where the fused form applies.
         self.fuse_shared_expert = True
+        # True: batches of up to ops.ROUTE_GATE_MAX_TOKENS tokens compute the
+        # router projection inside the routing kernel (one launch instead of
+        # a cuBLAS GEMM plus the router).  Off by default: its fp32
+        # accumulation order differs from cuBLAS's, so a bf16 logit can differ
+        # by one unit and with it the routing of that token.
+        self.fuse_router_gate = False
 
         # Kernel entry points; tests may substitute an object with the same
         # functions to exercise the host logic without a GPU.
@@ -690,7 +696,28 @@ class ExpertParallelMoE(nn.Module):
         ``shared``: include the shared expert (one more grouped expert)."""
         if x.size(0) == 0:
             return torch.zeros_like(x)
+        if (self.fuse_router_gate and not shared and self._ops is _native_ops and x.is_cuda
+                and x.size(0) <= _native_ops.ROUTE_GATE_MAX_TOKENS
+                and x.dtype == torch.bfloat16 and self.gate.weight.dtype == torch.bfloat16):
+            return self._forward_fused_gate(x)
         return self._forward_from_logits(x, self.gate(x), shared=shared)
+
+    def _forward_fused_gate(self, x: torch.Tensor) -> torch.Tensor:
+        """The router projection inside the routing launch (fuse_router_gate)."""
+        num_tokens = x.size(0)
+        self._check_inputs(x)
+        weights, ids, logits = self._ops.route_gate_topk(x, self.gate.weight, self.top_k,
+                                                         self.norm_topk_prob)
+        if self._use_tiny_path(num_tokens, logits):
+            # The tiny kernels route from the logits themselves (same routine).
+            return self._forward_from_logits(x, logits)
+        stats = self._device_stats(x.device)
+        flat_w = weights.view(-1)
+        packed = self._pack(ids.view(-1), flat_w, capacity=self._capacity(num_tokens),
+                            stats=stats)
+        y = self._run_experts(x, flat_w, packed, self.top_k)
+        self.total_assignment_count += ids.numel()
+        return self._combine_expert_routes(y, packed.combine_rows, num_tokens, self.top_k)
 
     def _forward_from_logits(self, x: torch.Tensor, logits: torch.Tensor,
                              shared: bool = False) -> torch.Tensor:

@@ -70,6 +70,35 @@ def route_topk(logits: torch.Tensor, top_k: int, renormalize: bool,
     return weights, ids
 
 
+# Largest batch b200moe_route_gate_topk takes.
+ROUTE_GATE_MAX_TOKENS = 64
+_GATE_SYNC: dict[torch.device, torch.Tensor] = {}
+
+
+def route_gate_topk(x: torch.Tensor, gate_w: torch.Tensor, top_k: int, renormalize: bool
+                    ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Router projection + softmax top-k (+ renorm) in one launch for
+    <= ROUTE_GATE_MAX_TOKENS tokens -> (bf16 weights, int64 ids, bf16 logits)."""
+    _require_cuda(x, gate_w)
+    if x.dtype != torch.bfloat16 or gate_w.dtype != torch.bfloat16:
+        raise TypeError("the fused router projection takes bf16 activations and gate weights")
+    x = x.contiguous()
+    gate_w = gate_w.contiguous()
+    tokens, hidden = x.shape
+    experts = gate_w.size(0)
+    device = x.device
+    sync = _GATE_SYNC.get(device)
+    if sync is None:
+        sync = torch.zeros(ROUTE_GATE_MAX_TOKENS // 8, device=device, dtype=torch.int32)
+        _GATE_SYNC[device] = sync
+    logits = torch.empty((tokens, experts), device=device, dtype=torch.bfloat16)
+    weights = torch.empty((tokens, top_k), device=device, dtype=torch.bfloat16)
+    ids = torch.empty((tokens, top_k), device=device, dtype=torch.int64)
+    call("b200moe_route_gate_topk", _p(x), hidden, _p(gate_w), tokens, experts, top_k,
+         int(bool(renormalize)), _p(logits), _p(weights), _p(ids), _p(sync), _stream(x))
+    return weights, ids, logits
+
+
 @dataclass
 class PackedRoutes:
     """Expert-major layout of a flat route array (see b200moe_pack_routes)."""

@@ -126,6 +126,29 @@ B200MOE_API int b200moe_route_topk_shared(const void *logits, int logits_dtype,
                                           int renormalize, const void *shared_logits,
                                           void *weights, int64_t *expert_ids, void *stream);
 
+/*
+ * The router projection fused with b200moe_route_topk, for small batches
+ * (num_tokens <= B200MOE_ROUTE_GATE_MAX_TOKENS).  Replaces the bf16 gate
+ * F.linear of moe.py:871 (linear.py:51) plus the routing of moe.py:872-878.
+ * logits[t, e] = bf16(sum_h x[t, h] * gate_w[e, h]) accumulated in fp32 in a
+ * fixed order (16-byte vectors l, l + 32, ... per lane, then a butterfly over
+ * the warp); cuBLAS accumulates in its own order, so a logit can differ from
+ * the reference's by one bf16 unit where the fp32 sums straddle a rounding
+ * boundary -- the routing of such tokens can then differ.  The routing of the
+ * written logits is exactly b200moe_route_topk's.
+ *   x        [num_tokens, hidden] bf16 (hidden % 8 == 0, <= 4096)
+ *   gate_w   [num_experts, hidden] bf16
+ *   logits   [num_tokens, num_experts] bf16 out
+ *   weights  [num_tokens, top_k] bf16 out;  expert_ids [num_tokens, top_k] int64 out
+ *   sync     int32 [ceil(num_tokens / 8)], zero before the first call; the
+ *            kernel leaves it zero (one buffer serves calls in stream order)
+ */
+#define B200MOE_ROUTE_GATE_MAX_TOKENS 64
+B200MOE_API int b200moe_route_gate_topk(const void *x, int hidden, const void *gate_w,
+                                        int64_t num_tokens, int num_experts, int top_k,
+                                        int renormalize, void *logits, void *weights,
+                                        int64_t *expert_ids, int32_t *sync, void *stream);
+
 /* Scratch bytes b200moe_pack_routes needs for `num_routes` routes. */
 B200MOE_API size_t b200moe_pack_scratch_bytes(int64_t num_routes, int num_experts);
 
