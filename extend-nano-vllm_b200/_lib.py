@@ -61,6 +61,8 @@ SIGNATURES: dict[str, tuple] = {
                                     _L, _P, _P, _P, _P]),
     "b200moe_expert_down": (_I, [_I, _P, _I, _I, _P, _I, _P, _P, _L, _L, _L, _P, _L, _P, _P,
                                  _P, _P]),
+    "b200moe_expert_down_scatter": (_I, [_I, _P, _I, _I, _P, _I, _P, _P, _L, _L, _P, _L, _P,
+                                         _P, _I, _L, _P, _P, _L, _P]),
     "b200moe_decode_tiny": (_I, [_P, _I, _P, _L, _I, _I, _I, _I, _I, _P, _P, _I, _P, _I, _P, _P,
                                  _P, _P]),
     "b200moe_combine": (_I, [_P, _L, _P, _L, _I, _I, _I, _P, _I, _P]),
@@ -83,6 +85,7 @@ SIGNATURES: dict[str, tuple] = {
     "b200moe_nvl_receive": (_I, [_I, _I, _P, _P, _L, _P, _P, _P, _P, _P, _P, _P]),
     "b200moe_nvl_return": (_I, [_P, _I, _P, _P, _P, _L, _L, _I, _I, _P, _P, _P]),
     "b200moe_nvl_wait_return": (_I, [_I, _I, _P, _P, _P]),
+    "b200moe_nvl_return_signal": (_I, [_I, _I, _P, _P, _P]),
 }
 NVL_LAYOUT_WORDS = 10
 NVL_ROUTE_CAP = 8  # layout word: route records per source region

@@ -134,7 +134,7 @@ int launch_combine(const void *y, int64_t num_rows, const int32_t *route_rows,
   const int threads = 256;
   const int64_t blocks = (threads_total + threads - 1) / threads;
   const auto *yp = static_cast<const __nv_bfloat16 *>(y);
-  const bool batch = num_tokens <= kCombineBatchTokens || top_k <= 8;
+  const bool batch = num_tokens <= kCombineBatchTokens;
 #define B200_COMBINE(OUT)                                                                      \
   if (batch)                                                                                   \
     B200_LAUNCH_PDL(kPdlCombine, combine_kernel<Acc, OUT, true>, dim3(blocks), dim3(threads),  \

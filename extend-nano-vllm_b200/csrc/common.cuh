@@ -255,6 +255,36 @@ struct RowSource {
   int64_t num_routes;
 };
 
+// Where a down projection writes its route rows when they do not go to y in
+// route order: route r's row (n_out bf16 values) goes to buffer base[rank[r]]
+// at byte offset `offset`, row row[r] (row < rows).  The expert-parallel
+// exchange uses it to write each received route's result straight into its
+// source's return buffer (peer memory) from the GEMM epilogue.  ranks == 0:
+// rows go to y.
+constexpr int kMaxScatterRanks = 16;
+struct RowScatter {
+  uint64_t base[kMaxScatterRanks];
+  const int32_t *rank = nullptr;
+  const int32_t *row = nullptr;
+  int64_t offset = 0;
+  int64_t rows = 0;
+  int ranks = 0;
+};
+
+// The destination row of route r under `sc` (null when out of range, which
+// sets the status word), or y's row r when scattering is off.
+__device__ __forceinline__ __nv_bfloat16 *scatter_row(const RowScatter &sc, __nv_bfloat16 *y,
+                                                      int64_t r, int n_out) {
+  if (sc.ranks == 0) return y + r * n_out;
+  const int d = sc.rank[r];
+  const int64_t row = sc.row[r];
+  if (d < 0 || d >= sc.ranks || row < 0 || row >= sc.rows) {
+    atomicOr(&g_status, kStatusIndex);
+    return nullptr;
+  }
+  return reinterpret_cast<__nv_bfloat16 *>(sc.base[d] + sc.offset) + row * n_out;
+}
+
 // Four rows r0..r3 (64 columns from c0) of a 2-D tensor whose map has a
 // one-row box, written as consecutive 128-byte rows at dst (swizzled like a
 // tile load).  Used to read routed rows of the token matrix directly.

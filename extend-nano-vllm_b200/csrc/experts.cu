@@ -18,14 +18,14 @@ int tc_gate_up(const RowSource &src, int hidden, int inter, const void *w13, int
 int tc_down(const void *act, int hidden, int inter, const void *w2, int num_local,
             const int32_t *row_route, const void *route_weights, int64_t num_routes,
             int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
-            const int32_t *counters, void *y, cudaStream_t s);
+            const int32_t *counters, void *y, const RowScatter *scatter, cudaStream_t s);
 int tcs_gate_up(const RowSource &src, int hidden, int inter, const void *w13, int num_local,
                 int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
                 const int32_t *counters, void *act, cudaStream_t s);
 int tcs_down(const void *act, int hidden, int inter, const void *w2, int num_local,
              const int32_t *row_route, const void *route_weights, int64_t num_routes,
              int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
-             const int32_t *counters, void *y, cudaStream_t s);
+             const int32_t *counters, void *y, const RowScatter *scatter, cudaStream_t s);
 int tct_gate_up(const void *x_packed, int hidden, int inter, const void *w13, int num_local,
                 int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
                 const int32_t *counters, void *act, cudaStream_t s);
@@ -146,10 +146,10 @@ int b200moe_expert_down(int engine, const void *act, int hidden, int inter, cons
                        max_expert_rows, mtiles, max_mtiles, counters, y, s);
   if (engine == B200MOE_ENGINE_TCGEN05_SWAP)
     return tcs_down(act, hidden, inter, w2, num_local_experts, row_route, route_weights,
-                    num_routes, row_capacity, mtiles, max_mtiles, counters, y, s);
+                    num_routes, row_capacity, mtiles, max_mtiles, counters, y, nullptr, s);
   if (engine == B200MOE_ENGINE_TCGEN05_WIDE)
     return tc_down(act, hidden, inter, w2, num_local_experts, row_route, route_weights,
-                   num_routes, row_capacity, mtiles, max_mtiles, counters, y, s);
+                   num_routes, row_capacity, mtiles, max_mtiles, counters, y, nullptr, s);
   if (engine == B200MOE_ENGINE_TCGEN05_PAIR) {
     B200_ARG(chunks != nullptr, "the two-SM engine needs the row-chunk list of pack_routes");
     return tcp_down(act, hidden, inter, w2, num_local_experts, row_route, route_weights,
@@ -157,6 +157,50 @@ int b200moe_expert_down(int engine, const void *act, int hidden, int inter, cons
   }
   set_error("unknown engine %d", engine);
   return B200MOE_EINVAL;
+}
+
+int b200moe_expert_down_scatter(int engine, const void *act, int hidden, int inter,
+                                const void *w2, int num_local_experts, const int32_t *row_route,
+                                const void *route_weights, int64_t num_routes,
+                                int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
+                                const int32_t *counters, const uint64_t *dst_bases,
+                                int dst_ranks, int64_t dst_offset, const int32_t *dst_rank,
+                                const int32_t *dst_row, int64_t dst_rows, void *stream) {
+  using namespace b200moe;
+  B200_ARG(hidden > 0 && inter > 0 && num_local_experts > 0, "bad shape");
+  B200_UNSUPPORTED(hidden % 16 == 0 && inter % 16 == 0,
+                   "hidden (%d) and intermediate (%d) sizes must be multiples of 16", hidden, inter);
+  B200_ARG(dst_ranks >= 1 && dst_ranks <= kMaxScatterRanks, "dst_ranks must be in [1, %d]",
+           kMaxScatterRanks);
+  B200_ARG(dst_rows >= 0 && dst_rows <= 0xffffff, "dst_rows must be < 2^24");
+  B200_ARG(dst_offset >= 0 && dst_offset % 16 == 0, "dst_offset must be a multiple of 16");
+  if (num_routes == 0 || max_mtiles == 0) return B200MOE_OK;
+  B200_ARG(act && w2 && row_route && route_weights && mtiles && counters && dst_bases &&
+               dst_rank && dst_row,
+           "null pointer argument");
+  B200_ARG(aligned16(act) && aligned16(w2), "act, w2 must be 16-byte aligned");
+  RowScatter sc;
+  for (int i = 0; i < kMaxScatterRanks; ++i) sc.base[i] = 0;
+  for (int i = 0; i < dst_ranks; ++i) {
+    B200_ARG(dst_bases[i] != 0 && dst_bases[i] % 16 == 0,
+             "destination buffer %d is null or not 16-byte aligned", i);
+    sc.base[i] = dst_bases[i];
+  }
+  sc.rank = dst_rank;
+  sc.row = dst_row;
+  sc.offset = dst_offset;
+  sc.rows = dst_rows;
+  sc.ranks = dst_ranks;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  engine = resolve_engine(engine, num_routes);
+  if (engine == B200MOE_ENGINE_TCGEN05_SWAP)
+    return tcs_down(act, hidden, inter, w2, num_local_experts, row_route, route_weights,
+                    num_routes, row_capacity, mtiles, max_mtiles, counters, nullptr, &sc, s);
+  if (engine == B200MOE_ENGINE_TCGEN05_WIDE)
+    return tc_down(act, hidden, inter, w2, num_local_experts, row_route, route_weights,
+                   num_routes, row_capacity, mtiles, max_mtiles, counters, nullptr, &sc, s);
+  set_error("scattered down rows need the tcgen05 wide or swap-AB engine (got %d)", engine);
+  return B200MOE_EUNSUPPORTED;
 }
 
 }  // extern "C"

@@ -74,6 +74,8 @@ struct Args {
   const int32_t *token_of_route;
   int top_k;
   int64_t x_rows;
+  // down only: rows to other buffers instead of out (ranks == 0: out).
+  RowScatter scatter;
 };
 
 __device__ __forceinline__ void store16_bf16(__nv_bfloat16 *dst, const float (&v)[16], int valid) {
@@ -116,7 +118,8 @@ __device__ __forceinline__ void tie16(float (&v)[16]) {
 template <bool kGateUp, int BN>
 __global__ void __launch_bounds__(THREADS, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
-                        const __grid_constant__ CUtensorMap tmB, const Args args) {
+                        const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ Args args) {
   constexpr int STAGES = Cfg<BN>::STAGES;
   constexpr int B_BYTES = Cfg<BN>::B_BYTES;
   constexpr int STAGE_BYTES = Cfg<BN>::STAGE_BYTES;
@@ -301,6 +304,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       } else {
         int32_t route = -1;
         float rw = 0.f;
+        __nv_bfloat16 *row_dst = nullptr;
         if (valid) {
           route = args.row_route[row];
           if (route < 0 || route >= args.num_routes) {
@@ -308,6 +312,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             route = -1;
           } else {
             rw = __bfloat162float(args.route_w[route]);
+            row_dst = scatter_row(args.scatter, args.out, route, args.n_out);
           }
         }
         const int col0 = n * BN;
@@ -349,12 +354,12 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int it = 0; it < 8; ++it) {
             const int r = it * 4 + (lane >> 3);
             const int sl = lane & 7;
-            const int r_route = __shfl_sync(0xffffffffu, route, r);
+            auto *r_dst = reinterpret_cast<__nv_bfloat16 *>(__shfl_sync(
+                0xffffffffu, reinterpret_cast<unsigned long long>(row_dst), r));
             const uint4 o = stage_w[r * 8 + (sl ^ (r & 7))];
             const int col = col0 + c + sl * 8;
-            if (r_route >= 0 && col < args.n_out)
-              *reinterpret_cast<uint4 *>(args.out + static_cast<int64_t>(r_route) * args.n_out +
-                                         col) = o;
+            if (r_dst != nullptr && col < args.n_out)
+              *reinterpret_cast<uint4 *>(r_dst + col) = o;
           }
           __syncwarp();
         }
@@ -504,7 +509,7 @@ template <int BN>
 int tc_down_bn(const void *act, int hidden, int inter, const void *w2, int num_local,
                const int32_t *row_route, const void *route_weights, int64_t num_routes,
                int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
-               const int32_t *counters, void *y, cudaStream_t s) {
+               const int32_t *counters, void *y, const RowScatter *scatter, cudaStream_t s) {
   using namespace tcg;
   CUtensorMap ma, mb;
   const uint64_t da[2] = {static_cast<uint64_t>(inter), static_cast<uint64_t>(row_capacity)};
@@ -534,6 +539,7 @@ int tc_down_bn(const void *act, int hidden, int inter, const void *w2, int num_l
   a.token_of_route = nullptr;
   a.top_k = 1;
   a.x_rows = 0;
+  if (scatter) a.scatter = *scatter;
   return launch<false, BN>(ma, mb, a, s);
 }
 
@@ -554,15 +560,17 @@ int tc_gate_up(const RowSource &src, int hidden, int inter, const void *w13, int
 int tc_down(const void *act, int hidden, int inter, const void *w2, int num_local,
             const int32_t *row_route, const void *route_weights, int64_t num_routes,
             int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
-            const int32_t *counters, void *y, cudaStream_t s) {
+            const int32_t *counters, void *y, const RowScatter *scatter, cudaStream_t s) {
   switch (pick_bn(num_routes)) {
     case 256:
       return tc_down_bn<256>(act, hidden, inter, w2, num_local, row_route, route_weights,
-                             num_routes, row_capacity, mtiles, max_mtiles, counters, y, s);
+                             num_routes, row_capacity, mtiles, max_mtiles, counters, y, scatter,
+                             s);
     case 128:
     default:
       return tc_down_bn<128>(act, hidden, inter, w2, num_local, row_route, route_weights,
-                             num_routes, row_capacity, mtiles, max_mtiles, counters, y, s);
+                             num_routes, row_capacity, mtiles, max_mtiles, counters, y, scatter,
+                             s);
   }
 }
 

@@ -69,6 +69,8 @@ struct Args {
   const int32_t *token_of_route;
   int top_k;
   int64_t x_rows;
+  // down only: rows to other buffers instead of out (ranks == 0: out).
+  RowScatter scatter;
 };
 
 __device__ __forceinline__ void epi_bar() {
@@ -78,7 +80,7 @@ __device__ __forceinline__ void epi_bar() {
 template <bool kGateUp>
 __global__ void __launch_bounds__(THREADS, 1)
     swapab_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
-                  const Args args) {
+                  const __grid_constant__ Args args) {
   using C = Cfg<kGateUp>;
   constexpr int STAGES = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -255,8 +257,19 @@ __global__ void __launch_bounds__(THREADS, 1)
             atomicOr(&g_status, kStatusIndex);
             r = -1;
           }
-          s_route[et] = r;
           s_w[et] = r >= 0 ? __bfloat162float(args.route_w[r]) : 0.f;
+          if (r >= 0 && args.scatter.ranks != 0) {
+            const int d = args.scatter.rank[r];
+            const int64_t row = args.scatter.row[r];
+            if (d < 0 || d >= args.scatter.ranks || row < 0 || row >= args.scatter.rows ||
+                row > 0xffffff) {
+              atomicOr(&g_status, kStatusIndex);
+              r = -1;
+            } else {
+              r = (d << 24) | static_cast<int32_t>(row);
+            }
+          }
+          s_route[et] = r;
         }
         epi_bar();
       }
@@ -289,9 +302,17 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int n = c + i;
             if (fvalid && n < rows) {
               const int32_t r = s_route[n];
-              if (r >= 0)
-                args.out[static_cast<int64_t>(r) * args.n_out + f] =
-                    __float2bfloat16_rn(v[i] * s_w[n]);
+              if (r >= 0) {
+                // Scattering: s_route holds rank << 24 | row (checked when
+                // the tile's routes were read).
+                __nv_bfloat16 *dst =
+                    args.scatter.ranks == 0
+                        ? args.out + static_cast<int64_t>(r) * args.n_out
+                        : reinterpret_cast<__nv_bfloat16 *>(args.scatter.base[r >> 24] +
+                                                            args.scatter.offset) +
+                              static_cast<int64_t>(r & 0xffffff) * args.n_out;
+                dst[f] = __float2bfloat16_rn(v[i] * s_w[n]);
+              }
             }
           }
         }
@@ -377,7 +398,7 @@ int tcs_gate_up(const RowSource &src, int hidden, int inter, const void *w13, in
 int tcs_down(const void *act, int hidden, int inter, const void *w2, int num_local,
              const int32_t *row_route, const void *route_weights, int64_t num_routes,
              int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
-             const int32_t *counters, void *y, cudaStream_t s) {
+             const int32_t *counters, void *y, const RowScatter *scatter, cudaStream_t s) {
   using namespace tcs;
   CUtensorMap mw, mx;
   const uint64_t dw[3] = {static_cast<uint64_t>(inter), static_cast<uint64_t>(hidden),
@@ -407,6 +428,7 @@ int tcs_down(const void *act, int hidden, int inter, const void *w2, int num_loc
   a.token_of_route = nullptr;
   a.top_k = 1;
   a.x_rows = 0;
+  if (scatter) a.scatter = *scatter;
   return launch<false>(mw, mx, a, s);
 }
 

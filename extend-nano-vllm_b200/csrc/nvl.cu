@@ -375,6 +375,16 @@ __global__ void __launch_bounds__(256) nvl_return_kernel(
   retire_and_signal(peers, l, kPhaseReturn, rank, ep_size, false);
 }
 
+// Destination, one CTA: the received routes' rows were written into the
+// sources' return buffers by the down GEMM's epilogue (b200moe_expert_down_scatter,
+// earlier in this stream); publish the return phase.
+__global__ void nvl_signal_return_kernel(int rank, int ep_size,
+                                         const __grid_constant__ Peers peers, NvlLayout l) {
+  pdl_trigger();
+  pdl_wait();
+  retire_and_signal(peers, l, kPhaseReturn, rank, ep_size, false);
+}
+
 // Source, one CTA: wait until every destination returned its rows.
 __global__ void nvl_return_wait_kernel(int rank, int ep_size, const __grid_constant__ Peers peers, NvlLayout l) {
   pdl_trigger();
@@ -593,6 +603,22 @@ int b200moe_nvl_return(const void *y, int hidden, const int32_t *src_rank,
   B200_LAUNCH_PDL(kPdlExchange, nvl_return_kernel, dim3(grid_for(max_routes, 8)), dim3(256), 0, s,
                   static_cast<const __nv_bfloat16 *>(y), hidden, src_rank, src_route,
                   route_count, max_routes, max_source_routes, rank, ep_size, p, *l);
+  B200_LAUNCHED();
+  return B200MOE_OK;
+}
+
+int b200moe_nvl_return_signal(int rank, int ep_size, const uint64_t *peer_bases,
+                              const int64_t *layout, void *stream) {
+  using namespace b200moe;
+  B200_NVL_CHECK(ep_size, rank);
+  B200_ARG(peer_bases && layout, "null pointer argument");
+  Peers p;
+  const NvlLayout *l = nullptr;
+  const int rc = load_peers(p, l, peer_bases, layout, ep_size);
+  if (rc != B200MOE_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  B200_LAUNCH_PDL(kPdlExchange, nvl_signal_return_kernel, dim3(1), dim3(32), 0, s, rank, ep_size,
+                  p, *l);
   B200_LAUNCHED();
   return B200MOE_OK;
 }

@@ -319,12 +319,19 @@ class NvlinkExchange:
             hint = None
             weights = weights[:received]
             token_of_route = token_of_route[:received]
-        if packed.num_routes:
-            y = layer._run_experts(bufs.tokens_view(), weights, packed, 1, token_of_route,
-                                   routes_hint=hint)
+        if packed.num_routes and getattr(ops, "NVL_DIRECT_RETURN", False):
+            # Rows go to the sources from the down GEMM's epilogue.
+            layer._run_experts(bufs.tokens_view(), weights, packed, 1, token_of_route,
+                               routes_hint=hint, scatter=(src_rank, src_route, bufs))
+            ops.nvl_return_signal(layer.ep_rank, bufs)
         else:
-            y = torch.empty((0, layer.hidden_size), device=self.x.device, dtype=torch.bfloat16)
-        ops.nvl_return(y, src_rank, src_route, count, layer.ep_rank, bufs)
+            if packed.num_routes:
+                y = layer._run_experts(bufs.tokens_view(), weights, packed, 1, token_of_route,
+                                       routes_hint=hint)
+            else:
+                y = torch.empty((0, layer.hidden_size), device=self.x.device,
+                                dtype=torch.bfloat16)
+            ops.nvl_return(y, src_rank, src_route, count, layer.ep_rank, bufs)
         layer.ep_all_to_all_count += 1
 
     # Phase 4: wait for this rank's rows, combine them in slot order.

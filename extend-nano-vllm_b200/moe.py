@@ -587,7 +587,8 @@ class ExpertParallelMoE(nn.Module):
     def _run_experts(self, x: torch.Tensor, flat_weights: torch.Tensor, packed, top_k: int,
                      token_of_route: torch.Tensor | None = None,
                      routes_hint: int | None = None,
-                     weights: tuple[torch.Tensor, torch.Tensor] | None = None) -> torch.Tensor:
+                     weights: tuple[torch.Tensor, torch.Tensor] | None = None,
+                     scatter: tuple | None = None) -> torch.Tensor | None:
         """Grouped gate/up + SwiGLU and grouped down -> y [num_routes, H] (route order).
 
         ``routes_hint``: the expected number of routes when ``packed`` is
@@ -595,7 +596,9 @@ class ExpertParallelMoE(nn.Module):
         it picks the tcgen05 variant and the row-gather strategy, and the
         streaming engine (whose route bound is compiled in) is not used.
         ``weights``: (w13, w2) to use instead of the local experts' (the
-        routed + shared storage)."""
+        routed + shared storage).  ``scatter``: (src_rank, src_route, bufs)
+        of the NVLink exchange: the down rows go straight to the sources'
+        return buffers (tcgen05 wide / swap-AB down) and None is returned."""
         w13, w2 = (self.gate_up_proj, self.down_proj) if weights is None else weights
         routes = packed.num_routes if routes_hint is None else max(1, int(routes_hint))
         engine = self._engine(routes)
@@ -619,7 +622,14 @@ class ExpertParallelMoE(nn.Module):
         if timer is not None:
             timer.end("gate_up")
             timer.begin("down")
-        y = ops.expert_down(engine, act, w2, packed, flat_weights, x.size(0))
+        if scatter is not None:
+            down_engine = (engine if engine in (_lib.ENGINE_TCGEN05_WIDE, _lib.ENGINE_TCGEN05_SWAP)
+                           else _lib.ENGINE_TCGEN05_SWAP if routes <= 4096
+                           else _lib.ENGINE_TCGEN05_WIDE)
+            ops.expert_down_scatter(down_engine, act, w2, packed, flat_weights, *scatter)
+            y = None
+        else:
+            y = ops.expert_down(engine, act, w2, packed, flat_weights, x.size(0))
         if timer is not None:
             timer.end("down")
         return y

@@ -9,6 +9,7 @@ graphs (no host synchronisation happens inside them).
 from __future__ import annotations
 
 import ctypes
+import os
 from dataclasses import dataclass
 
 import torch
@@ -443,6 +444,32 @@ def nvl_return(y: torch.Tensor, src_rank: torch.Tensor, src_route: torch.Tensor,
     call("b200moe_nvl_return", _p(y), bufs.hidden, _p(src_rank), _p(src_route), _p(count),
          y.size(0), bufs.max_tokens * bufs.top_k, rank, bufs.ep_size, bufs.peer_bases,
          bufs.layout_ptr, bufs.stream_ptr())
+
+
+def nvl_return_signal(rank: int, bufs) -> None:
+    """Publish the return phase after expert_down_scatter wrote the rows."""
+    call("b200moe_nvl_return_signal", rank, bufs.ep_size, bufs.peer_bases, bufs.layout_ptr,
+         bufs.stream_ptr())
+
+
+# The NVLink exchange writes each received route's down-projection row
+# straight into its source's return buffer from the GEMM epilogue
+# (expert_down_scatter) instead of copying y afterwards (nvl_return).
+# B200MOE_NVL_DIRECT_RETURN=0 keeps the copy.
+NVL_DIRECT_RETURN = os.environ.get("B200MOE_NVL_DIRECT_RETURN", "1") != "0"
+
+
+def expert_down_scatter(engine: int, act: torch.Tensor, w2: torch.Tensor, packed: PackedRoutes,
+                        route_weights: torch.Tensor, src_rank: torch.Tensor,
+                        src_route: torch.Tensor, bufs) -> None:
+    """Route-weighted down projection whose route rows go to the sources'
+    return buffers (rank src_rank[r], row src_route[r]) of the exchange."""
+    num_local, hidden, inter = w2.shape
+    call("b200moe_expert_down_scatter", engine, _p(act), hidden, inter, _p(w2), num_local,
+         _p(packed.row_route), _p(route_weights), packed.num_routes, packed.row_capacity,
+         _p(packed.mtiles), packed.max_mtiles, _p(packed.counters), bufs.peer_bases,
+         bufs.ep_size, bufs.layout["returned"], _p(src_rank), _p(src_route),
+         bufs.max_tokens * bufs.top_k, _stream(act))
 
 
 def nvl_wait_return(rank: int, bufs) -> None:

@@ -368,6 +368,27 @@ B200MOE_API int b200moe_expert_down(int engine, const void *act, int hidden, int
                         const int32_t *counters, void *y, void *stream);
 
 /*
+ * b200moe_expert_down writing each route's row into another buffer instead of
+ * y: route r's bf16 row goes to dst_bases[dst_rank[r]] + dst_offset bytes,
+ * row dst_row[r] (rows of H values, dst_row < dst_rows).  The expert-parallel
+ * exchange passes the ranks' exchange buffers (peer memory mapped with CUDA
+ * IPC) at their return region and the received routes' source rank / source
+ * route, so the rows land at their sources from the GEMM epilogue while
+ * later tiles compute, replacing the copy of b200moe_nvl_return (then
+ * b200moe_nvl_return_signal publishes the phase).  Same arithmetic as
+ * b200moe_expert_down.  Engines: TCGEN05 (the library picks), TCGEN05_WIDE,
+ * TCGEN05_SWAP.  Limits: dst_ranks <= 16, dst_rows < 2^24, dst_offset and
+ * the bases 16-byte aligned; an out-of-range rank or row sets the index
+ * status bit and the row is not written.
+ */
+B200MOE_API int b200moe_expert_down_scatter(
+    int engine, const void *act, int hidden, int inter, const void *w2, int num_local_experts,
+    const int32_t *row_route, const void *route_weights, int64_t num_routes,
+    int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles, const int32_t *counters,
+    const uint64_t *dst_bases, int dst_ranks, int64_t dst_offset, const int32_t *dst_rank,
+    const int32_t *dst_row, int64_t dst_rows, void *stream);
+
+/*
  * Fused expert path for tiny decode batches (num_tokens * top_k <= 16, no
  * capacity limit): router + gate/up + SwiGLU + down + route-order combine in
  * two launches.  Every CTA routes its token itself (same routine as
@@ -547,6 +568,17 @@ B200MOE_API int b200moe_nvl_return(const void *y, int hidden, const int32_t *src
                                    int64_t max_routes, int64_t max_source_routes, int rank,
                                    int ep_size, const uint64_t *peer_bases, const int64_t *layout,
                                    void *stream);
+
+/*
+ * The return phase without the copy: the received routes' rows were already
+ * written into the sources' return buffers by b200moe_expert_down_scatter
+ * (earlier in this stream, destinations = every rank's exchange buffer at the
+ * layout's `returned` offset, dst_rank/dst_row = the src_rank/src_route of
+ * b200moe_nvl_receive).  Publishes the phase to every source like
+ * b200moe_nvl_return does after its copies.
+ */
+B200MOE_API int b200moe_nvl_return_signal(int rank, int ep_size, const uint64_t *peer_bases,
+                                          const int64_t *layout, void *stream);
 
 /* Source: waits until every destination returned its rows. */
 B200MOE_API int b200moe_nvl_wait_return(int rank, int ep_size, const uint64_t *peer_bases,

@@ -85,9 +85,14 @@ CASES = [(2, (96, 160), {}), (4, (64, 1, 0, 300), {}), (2, (512, 512), {}),
          (2, (64, 200), {"expert_capacity": 12}), (8, (16,) * 8, {})]
 
 
+@pytest.mark.parametrize("direct", [True, False], ids=["epilogue-return", "copy-return"])
 @pytest.mark.parametrize("world,counts,kw", CASES)
 @torch.inference_mode()
-def test_exchange_matches_single_gpu_layer(world, counts, kw):
+def test_exchange_matches_single_gpu_layer(world, counts, kw, direct, monkeypatch):
+    """``direct``: the down GEMM writes the returned rows into the sources'
+    buffers (default) or y is copied there afterwards."""
+    from extend_nano_vllm_b200 import ops
+    monkeypatch.setattr(ops, "NVL_DIRECT_RETURN", direct)
     full, ranks = _layers(world, kw)
     bufs = _buffers(ranks, max(counts))
     dist_env.set_moe_token_counts(counts)
