@@ -1240,7 +1240,8 @@ def e2e(args) -> None:
               "config": {"model": f"Qwen3-30B-A3B architecture, {args.e2e_layers} layers",
                          "requests": args.e2e_requests, "prompt_tokens": args.e2e_prompt,
                          "output_tokens": args.e2e_output, "parallelism": f"dp{dp}xep{dp}",
-                         "moe_backend": ("all_to_all_nvlink (this repository)"
+                         "moe_backend": ("replicated, one GPU" if dp == 1 else
+                                         "all_to_all_nvlink (this repository)"
                                          if args.e2e == "b200" else
                                          "allgather_reduce (reference)"),
                          "kvcache_block_size": 256, "decode_cuda_graphs": True},

@@ -297,8 +297,13 @@ class NvlinkExchange:
         """Host bound on the routes this rank can receive in this call."""
         layer = self.layer
         counts = dist_env.get_context().moe_token_counts
-        tokens = (sum(counts) if counts is not None and len(counts) == layer.ep_size
-                  else layer.ep_size * self.tokens)
+        peer_cap = getattr(layer, "nvl_graph_peer_tokens", None)
+        if counts is not None and len(counts) == layer.ep_size:
+            tokens = sum(counts)
+        elif peer_cap is not None:
+            tokens = self.tokens + (layer.ep_size - 1) * max(int(peer_cap), self.tokens)
+        else:
+            tokens = layer.ep_size * self.tokens
         per_token = min(layer.top_k, layer.num_local_experts)
         return max(1, min(self.bufs.max_routes, tokens * per_token))
 

@@ -281,6 +281,13 @@ class ExpertParallelMoE(nn.Module):
         # Largest batch (tokens per rank) the NVLink exchange buffers hold
         # ("all_to_all_nvlink"); None: nvl.DEFAULT_MAX_TOKENS.
         self.nvl_max_tokens: int | None = None
+        # Under CUDA-graph capture without coordinated per-rank token counts,
+        # the exchange sizes its temporaries for every peer holding as many
+        # tokens as this rank (the reference's equal-batch contract).  Set to
+        # the largest batch any peer may replay with (e.g. the largest decode
+        # graph size) to let ranks replay graphs of different batch sizes in
+        # the same step.
+        self.nvl_graph_peer_tokens: int | None = None
         # Counters fed by kernels: host part + device accumulator
         # [local kept routes, dropped routes, dispatched tokens], read
         # (synchronising) on access.

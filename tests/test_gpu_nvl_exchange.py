@@ -154,3 +154,34 @@ def test_exchange_replays_from_one_cuda_graph(kw, counts):
         expected = full(torch.cat(xs))
         torch.cuda.synchronize()
         assert torch.equal(torch.cat(outs), expected), step
+
+
+@torch.inference_mode()
+def test_exchange_graph_sized_by_peer_token_bound():
+    """Without coordinated counts, a per-peer token bound
+    (nvl_graph_peer_tokens) sizes the captured temporaries, so ranks holding
+    different batch sizes replay one step correctly (the ranks' graphs need
+    not agree on sizes)."""
+    counts = (8, 64, 1, 40)
+    world = len(counts)
+    full, ranks = _layers(world, {})
+    for layer in ranks:
+        layer.nvl_graph_peer_tokens = max(counts)
+    bufs = _buffers(ranks, max(counts))
+    dist_env.set_moe_token_counts(None)
+    xs = [wl.hidden_states(c, SHAPE.hidden, seed=7 + r).to(DEV) for r, c in enumerate(counts)]
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        _exchange(ranks, bufs, xs)
+    torch.cuda.current_stream().wait_stream(stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        outs = _exchange(ranks, bufs, xs)
+    for step in range(2):
+        for r, x in enumerate(xs):
+            x.copy_(wl.hidden_states(counts[r], SHAPE.hidden, seed=200 + 10 * step + r).to(DEV))
+        graph.replay()
+        expected = full(torch.cat(xs))
+        torch.cuda.synchronize()
+        assert torch.equal(torch.cat(outs), expected), step
