@@ -420,3 +420,13 @@ def forward_reference_torch(x: torch.Tensor, gate_w: torch.Tensor, w13: torch.Te
         o = torch.nn.functional.linear(h, w2[e]) * w[tok, slot, None]
         out.index_add_(0, tok, o)
     return out
+
+
+def shared_expert_torch(x: torch.Tensor, w13_s: torch.Tensor, w2_s: torch.Tensor,
+                        gate_s: torch.Tensor) -> torch.Tensor:
+    """The shared expert term the reference adds after the routed output
+    (moe.py:1259-1262): sigmoid(x gate_s^T) * down(silu(gate) * up), with the
+    MLP of moe.py:231-234; bf16 torch operations as on the reference's path."""
+    gate, up = torch.nn.functional.linear(x, w13_s).chunk(2, dim=-1)
+    projected = torch.nn.functional.linear(torch.nn.functional.silu(gate) * up, w2_s)
+    return torch.sigmoid(torch.nn.functional.linear(x, gate_s)) * projected

@@ -81,6 +81,7 @@ def _exchange(ranks, bufs, xs):
 
 
 CASES = [(2, (96, 160), {}), (4, (64, 1, 0, 300), {}), (2, (512, 512), {}),
+         (2, (1536, 1024), {}),  # > 4096 received routes per rank: wide tiles
          (4, (200, 100, 50, 25), {"expert_capacity_factor": 1.0}),
          (2, (64, 200), {"expert_capacity": 12}), (8, (16,) * 8, {})]
 

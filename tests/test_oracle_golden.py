@@ -205,3 +205,19 @@ def test_reference_cpu_baseline_restatement_matches_golden(golden):
     out = mo.forward_reference_torch(x, gate, w13, w2, 2, True)
     np.testing.assert_array_equal(out.float().numpy(),
                                   mo.from_bf16_bits(golden["fwd_small_out"]).reshape(22, 128))
+
+
+def test_shared_expert_restatement_matches_golden(golden):
+    """The reference layer with a shared expert (moe.py:1259-1262) on its CPU
+    path: routed output plus the shared term, bit for bit."""
+    shape = wl.LayerShape("fwd-small", 128, 256, 8, 2)
+    w13, w2 = wl.expert_weights(shape, seed=21)
+    gate = wl.gate_weight(shape, seed=22).to(torch.bfloat16)
+    x = wl.hidden_states(22, shape.hidden, seed=23)
+    shared = wl.LayerShape("fwd-small-shared", 128, 256, 8, 2, shared_intermediate=256)
+    s13, s2, sg = wl.shared_expert_weights(shared, seed=24)
+    routed = mo.forward_reference_torch(x, gate, w13, w2, 2, True)
+    out = routed + mo.shared_expert_torch(x, s13, s2, sg)
+    np.testing.assert_array_equal(
+        out.float().numpy(),
+        mo.from_bf16_bits(golden["fwd_small_shared_out"]).reshape(22, 128))
