@@ -1190,6 +1190,7 @@ def e2e(args) -> None:
     launch: one spawned process per replica, a shared MoE group over all of
     them, prompts dealt round-robin, equal max_tokens, EOS ignored)."""
     import multiprocessing as mp
+    import shutil
     import socket
     import tempfile
     from queue import Empty
@@ -1234,6 +1235,7 @@ def e2e(args) -> None:
         if p.is_alive():
             p.terminate()
             p.join()
+    shutil.rmtree(root, ignore_errors=True)
     record = {"metric": "e2e decode tokens/s (offline generation, DP x EP)", "impl": args.e2e,
               "n_gpus": dp, "unit": "tokens/s", "higher_is_better": True,
               "data": "random-init weights, seeded uniform prompt token ids",
