@@ -72,3 +72,31 @@ def test_static_scratch_limit_is_the_scratch_rule_not_a_route_bound():
             _lib.call("b200moe_pack_routes_static_scratch", null, null, routes, 128, null, 0,
                       128, null, -1, 0, null, null, null, null, null, null, null, 0, null, null,
                       null)
+
+
+def test_argument_errors_of_the_fused_entry_points():
+    """The shared-expert, route+pack, fused-projection and scattered-down
+    entry points check their arguments before touching a device."""
+    null = ctypes.c_void_p(0)
+    fake = ctypes.c_void_p(256)  # checked for null only, never dereferenced here
+    with pytest.raises(NotImplementedError, match="top_k 32 > 31"):
+        _lib.call("b200moe_route_topk_shared", null, _lib.F32, 4, 64, 32, 1, fake, null, null,
+                  null)
+    with pytest.raises(ValueError, match="shared_logits is null"):
+        _lib.call("b200moe_route_topk_shared", null, _lib.F32, 4, 64, 8, 1, null, null, null,
+                  null)
+    with pytest.raises(ValueError, match="num_shared_experts"):
+        _lib.call("b200moe_pack_routes_shared", null, null, 16, 8, 8, null, 0, 8, -1, 32, null,
+                  null, null, null, fake, fake, null, 10, null, fake, null, null, 0, null)
+    with pytest.raises(ValueError, match="num_tokens \\* top_k"):
+        _lib.call("b200moe_route_pack", null, _lib.F32, 200, 128, 8, 1, null, null, null, 0,
+                  128, -1, 0, null, null, null, null, null, null, null, 0, null, null, null,
+                  null, 0, null)
+    with pytest.raises(NotImplementedError, match="at most 64 tokens"):
+        _lib.call("b200moe_route_gate_topk", null, 2048, null, 65, 128, 8, 1, null, null, null,
+                  null, null)
+    with pytest.raises(ValueError, match="dst_ranks"):
+        _lib.call("b200moe_expert_down_scatter", 0, null, 64, 64, null, 1, null, null, 1, 16,
+                  null, 1, null, null, 17, 0, null, null, 1, null)
+    with pytest.raises(ValueError, match="ep_size|rank"):
+        _lib.call("b200moe_nvl_return_signal", 3, 2, null, null, null)
