@@ -61,8 +61,6 @@ SIGNATURES: dict[str, tuple] = {
                                     _L, _P, _P, _P, _P]),
     "b200moe_expert_down": (_I, [_I, _P, _I, _I, _P, _I, _P, _P, _L, _L, _L, _P, _L, _P, _P,
                                  _P, _P]),
-    "b200moe_expert_down_combine": (_I, [_P, _I, _I, _P, _I, _P, _P, _L, _L, _P, _L, _P, _P,
-                                         _L, _I, _P, _P, _L, _P]),
     "b200moe_expert_down_scatter": (_I, [_I, _P, _I, _I, _P, _I, _P, _P, _L, _L, _P, _L, _P,
                                          _P, _I, _L, _P, _P, _L, _P]),
     "b200moe_decode_tiny": (_I, [_P, _I, _P, _L, _I, _I, _I, _I, _I, _P, _P, _I, _P, _I, _P, _P,

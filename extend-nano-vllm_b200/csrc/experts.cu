@@ -25,9 +25,7 @@ int tcs_gate_up(const RowSource &src, int hidden, int inter, const void *w13, in
 int tcs_down(const void *act, int hidden, int inter, const void *w2, int num_local,
              const int32_t *row_route, const void *route_weights, int64_t num_routes,
              int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
-             const int32_t *counters, void *y, const RowScatter *scatter, cudaStream_t s,
-             void *combine_out = nullptr, int32_t *combine_sync = nullptr,
-             int combine_k = 0);
+             const int32_t *counters, void *y, const RowScatter *scatter, cudaStream_t s);
 int tct_gate_up(const void *x_packed, int hidden, int inter, const void *w13, int num_local,
                 int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
                 const int32_t *counters, void *act, cudaStream_t s);
@@ -159,30 +157,6 @@ int b200moe_expert_down(int engine, const void *act, int hidden, int inter, cons
   }
   set_error("unknown engine %d", engine);
   return B200MOE_EINVAL;
-}
-
-int b200moe_expert_down_combine(const void *act, int hidden, int inter, const void *w2,
-                                int num_local_experts, const int32_t *row_route,
-                                const void *route_weights, int64_t num_routes,
-                                int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
-                                const int32_t *counters, void *y, int64_t num_tokens, int top_k,
-                                void *out, int32_t *sync, int64_t sync_words, void *stream) {
-  using namespace b200moe;
-  B200_ARG(hidden > 0 && inter > 0 && num_local_experts > 0, "bad shape");
-  B200_UNSUPPORTED(hidden % 16 == 0 && inter % 16 == 0,
-                   "hidden (%d) and intermediate (%d) sizes must be multiples of 16", hidden, inter);
-  B200_ARG(top_k >= 1 && num_tokens >= 0 && num_routes == num_tokens * top_k,
-           "num_routes must be num_tokens * top_k");
-  B200_UNSUPPORTED(num_routes <= 4096, "the fused combine runs on swap-AB tiles (<= 4096 routes)");
-  B200_ARG(sync_words >= num_tokens * ((hidden + 127) / 128),
-           "sync needs num_tokens * ceil(hidden / 128) words");
-  if (num_routes == 0 || max_mtiles == 0) return B200MOE_OK;
-  B200_ARG(act && w2 && row_route && route_weights && mtiles && counters && y && out && sync,
-           "null pointer argument");
-  B200_ARG(aligned16(act) && aligned16(w2), "act, w2 must be 16-byte aligned");
-  return tcs_down(act, hidden, inter, w2, num_local_experts, row_route, route_weights,
-                  num_routes, row_capacity, mtiles, max_mtiles, counters, y, nullptr,
-                  static_cast<cudaStream_t>(stream), out, sync, top_k);
 }
 
 int b200moe_expert_down_scatter(int engine, const void *act, int hidden, int inter,

@@ -71,20 +71,7 @@ struct Args {
   int64_t x_rows;
   // down only: rows to other buffers instead of out (ranks == 0: out).
   RowScatter scatter;
-  // down only, small batches with every route computed here: the CTA that
-  // writes the last route of a token for a feature block also sums the
-  // token's route rows (slot order, fp32) into combine_out [T, n_out] bf16.
-  // combine_sync: int32 [T][n_blocks] arrival counters, zero on entry and
-  // left zero.  Null: no combine.
-  __nv_bfloat16 *combine_out;
-  int32_t *combine_sync;
-  int combine_k;
 };
-
-__device__ __forceinline__ float ldcg_bf16(const __nv_bfloat16 *p) {
-  return __bfloat162float(
-      __ushort_as_bfloat16(__ldcg(reinterpret_cast<const unsigned short *>(p))));
-}
 
 __device__ __forceinline__ void epi_bar() {
   asm volatile("bar.sync 1, %0;" ::"n"(128 * EPI_GROUPS) : "memory");
@@ -109,8 +96,6 @@ __global__ void __launch_bounds__(THREADS, 1)
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
   int32_t *s_route = reinterpret_cast<int32_t *>(tmem_holder + 4);  // [NMAX]
   float *s_w = reinterpret_cast<float *>(s_route + NMAX);           // [NMAX]
-  int32_t *s_last = reinterpret_cast<int32_t *>(s_w + NMAX);        // [NMAX] tokens to sum
-  int *s_nlast = reinterpret_cast<int *>(s_last + NMAX);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -332,39 +317,6 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
       }
-      if (!kGateUp && args.combine_out != nullptr) {
-        // Route-order combine of the tokens whose last route this tile
-        // wrote (for this feature block): arrival counters per (token,
-        // block); the last arriver sums the token's k rows from L2.
-        __threadfence();
-        epi_bar();
-        if (et == 0) *s_nlast = 0;
-        epi_bar();
-        if (et < rows) {
-          const int32_t r = s_route[et];
-          if (r >= 0) {
-            const int64_t t = r / args.combine_k;
-            int32_t *cnt = args.combine_sync + t * args.n_blocks + fb;
-            if (atomicAdd(cnt, 1) == args.combine_k - 1) {
-              *cnt = 0;  // ready for the next call
-              s_last[atomicAdd(s_nlast, 1)] = static_cast<int32_t>(t);
-            }
-          }
-        }
-        __threadfence();
-        epi_bar();
-        const int nl = *s_nlast;
-        for (int i = grp; i < nl; i += EPI_GROUPS) {
-          const int64_t t = s_last[i];
-          if (fvalid) {
-            float sum = 0.f;
-            for (int sl = 0; sl < args.combine_k; ++sl)
-              sum += ldcg_bf16(args.out + (t * args.combine_k + sl) * args.n_out + f);
-            args.combine_out[t * args.n_out + f] = __float2bfloat16_rn(sum);
-          }
-        }
-        epi_bar();  // s_route, s_last and s_nlast are rewritten for the next tile
-      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&acc_empty[acc]));
@@ -440,17 +392,13 @@ int tcs_gate_up(const RowSource &src, int hidden, int inter, const void *w13, in
   a.token_of_route = src.token_of_route;
   a.top_k = src.top_k;
   a.x_rows = src.x_rows;
-  a.combine_out = nullptr;
-  a.combine_sync = nullptr;
-  a.combine_k = 0;
   return launch<true>(mw, mx, a, s);
 }
 
 int tcs_down(const void *act, int hidden, int inter, const void *w2, int num_local,
              const int32_t *row_route, const void *route_weights, int64_t num_routes,
              int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles,
-             const int32_t *counters, void *y, const RowScatter *scatter, cudaStream_t s,
-             void *combine_out, int32_t *combine_sync, int combine_k) {
+             const int32_t *counters, void *y, const RowScatter *scatter, cudaStream_t s) {
   using namespace tcs;
   CUtensorMap mw, mx;
   const uint64_t dw[3] = {static_cast<uint64_t>(inter), static_cast<uint64_t>(hidden),
@@ -481,9 +429,6 @@ int tcs_down(const void *act, int hidden, int inter, const void *w2, int num_loc
   a.top_k = 1;
   a.x_rows = 0;
   if (scatter) a.scatter = *scatter;
-  a.combine_out = static_cast<__nv_bfloat16 *>(combine_out);
-  a.combine_sync = combine_sync;
-  a.combine_k = combine_k;
   return launch<false>(mw, mx, a, s);
 }
 

@@ -595,8 +595,7 @@ class ExpertParallelMoE(nn.Module):
                      token_of_route: torch.Tensor | None = None,
                      routes_hint: int | None = None,
                      weights: tuple[torch.Tensor, torch.Tensor] | None = None,
-                     scatter: tuple | None = None,
-                     combine_tokens: int | None = None) -> torch.Tensor | None:
+                     scatter: tuple | None = None) -> torch.Tensor | None:
         """Grouped gate/up + SwiGLU and grouped down -> y [num_routes, H] (route order).
 
         ``routes_hint``: the expected number of routes when ``packed`` is
@@ -606,10 +605,7 @@ class ExpertParallelMoE(nn.Module):
         ``weights``: (w13, w2) to use instead of the local experts' (the
         routed + shared storage).  ``scatter``: (src_rank, src_route, bufs)
         of the NVLink exchange: the down rows go straight to the sources'
-        return buffers (tcgen05 wide / swap-AB down) and None is returned.
-        ``combine_tokens``: the down GEMM also runs the route-order combine
-        of that many tokens (swap-AB tiles; every route computed here) and
-        the combined [T, H] output is returned instead of y."""
+        return buffers (tcgen05 wide / swap-AB down) and None is returned."""
         w13, w2 = (self.gate_up_proj, self.down_proj) if weights is None else weights
         routes = packed.num_routes if routes_hint is None else max(1, int(routes_hint))
         engine = self._engine(routes)
@@ -639,8 +635,6 @@ class ExpertParallelMoE(nn.Module):
                            else _lib.ENGINE_TCGEN05_WIDE)
             ops.expert_down_scatter(down_engine, act, w2, packed, flat_weights, *scatter)
             y = None
-        elif combine_tokens is not None:
-            y = ops.expert_down_combine(act, w2, packed, flat_weights, combine_tokens, top_k)
         else:
             y = ops.expert_down(engine, act, w2, packed, flat_weights, x.size(0))
         if timer is not None:
@@ -777,25 +771,9 @@ class ExpertParallelMoE(nn.Module):
             packed = self._pack(ids.view(-1), weights.view(-1),
                                 capacity=self._capacity(num_tokens), stats=stats)
         flat_w = weights.view(-1)
-        self.total_assignment_count += ids.numel()
-        if self._fused_combine(num_tokens):
-            return self._run_experts(x, flat_w, packed, self.top_k, combine_tokens=num_tokens)
         y = self._run_experts(x, flat_w, packed, self.top_k)
+        self.total_assignment_count += ids.numel()
         return self._combine_expert_routes(y, packed.combine_rows, num_tokens, self.top_k)
-
-    def _fused_combine(self, num_tokens: int) -> bool:
-        """Small batches whose every route is computed on this rank (no
-        capacity, all experts local, bf16 output) run the combine inside the
-        swap-AB down GEMM."""
-        routes = num_tokens * self.top_k
-        return (self._ops is _native_ops
-                and num_tokens <= _native_ops.DOWN_COMBINE_MAX_TOKENS
-                and STREAM_ENGINE_MAX_ROUTES < routes <= 4096
-                and self.expert_engine in ("auto", "tcgen05", "tcgen05-swap")
-                and self.expert_capacity is None and self.expert_capacity_factor is None
-                and self.num_local_experts == self.num_experts
-                and self.expert_id_to_local is None and max(self.expert_start, 0) == 0
-                and not self.fp64_combine and not self.fp32_reduce)
 
     def _forward_with_shared(self, x: torch.Tensor, logits: torch.Tensor,
                              stats: torch.Tensor | None) -> torch.Tensor:

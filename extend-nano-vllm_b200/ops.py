@@ -289,33 +289,6 @@ def expert_down(engine: int, act: torch.Tensor, w2: torch.Tensor, packed: Packed
     return y
 
 
-# Largest batch whose route-order combine runs inside the down GEMM.
-DOWN_COMBINE_MAX_TOKENS = 64
-_COMBINE_SYNC: dict[torch.device, torch.Tensor] = {}
-
-
-def expert_down_combine(act: torch.Tensor, w2: torch.Tensor, packed: PackedRoutes,
-                        route_weights: torch.Tensor, num_tokens: int, top_k: int
-                        ) -> torch.Tensor:
-    """Swap-AB down projection with the route-order combine fused in
-    (every route computed here, <= DOWN_COMBINE_MAX_TOKENS tokens) -> out [T, H] bf16."""
-    num_local, hidden, inter = w2.shape
-    device = act.device
-    words = DOWN_COMBINE_MAX_TOKENS * ((hidden + 127) // 128)
-    sync = _COMBINE_SYNC.get(device)
-    if sync is None or sync.numel() < words:
-        sync = torch.zeros(max(words, DOWN_COMBINE_MAX_TOKENS * 32), device=device,
-                           dtype=torch.int32)
-        _COMBINE_SYNC[device] = sync
-    y = torch.empty((packed.num_routes, hidden), device=device, dtype=torch.bfloat16)
-    out = torch.empty((num_tokens, hidden), device=device, dtype=torch.bfloat16)
-    call("b200moe_expert_down_combine", _p(act), hidden, inter, _p(w2), num_local,
-         _p(packed.row_route), _p(route_weights), packed.num_routes, packed.row_capacity,
-         _p(packed.mtiles), packed.max_mtiles, _p(packed.counters), _p(y), num_tokens, top_k,
-         _p(out), _p(sync), sync.numel(), _stream(act))
-    return out
-
-
 TINY_MAX_ROUTES = 16
 
 

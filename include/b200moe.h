@@ -368,26 +368,6 @@ B200MOE_API int b200moe_expert_down(int engine, const void *act, int hidden, int
                         const int32_t *counters, void *y, void *stream);
 
 /*
- * b200moe_expert_down (TCGEN05_SWAP tiles, <= 4096 routes) followed by the
- * route-order combine in the same launch, for small batches in which every
- * route is computed here (no capacity limit, every expert local): y is
- * written as by b200moe_expert_down, and the CTA that writes the last of a
- * token's top_k routes for a 128-column block sums the token's rows in slot
- * order in fp32 (from L2) and stores the bf16 sum in out — the arithmetic of
- * b200moe_combine with route_rows = NULL, so out is the same bits.
- *   num_routes == num_tokens * top_k
- *   out  [num_tokens, hidden] bf16
- *   sync int32 [sync_words >= num_tokens * ceil(hidden / 128)], zero before the
- *        first call; the kernel leaves it zero (calls in stream order)
- */
-B200MOE_API int b200moe_expert_down_combine(
-    const void *act, int hidden, int inter, const void *w2, int num_local_experts,
-    const int32_t *row_route, const void *route_weights, int64_t num_routes,
-    int64_t row_capacity, const int32_t *mtiles, int64_t max_mtiles, const int32_t *counters,
-    void *y, int64_t num_tokens, int top_k, void *out, int32_t *sync, int64_t sync_words,
-    void *stream);
-
-/*
  * b200moe_expert_down writing each route's row into another buffer instead of
  * y: route r's bf16 row goes to dst_bases[dst_rank[r]] + dst_offset bytes,
  * row dst_row[r] (rows of H values, dst_row < dst_rows).  The expert-parallel
