@@ -18,7 +18,7 @@ namespace b200moe {
 namespace {
 
 constexpr int kMaxEp = 16;
-constexpr int kPlanThreads = 1024;
+constexpr int kPlanThreads = 512;
 
 struct Offsets {
   int32_t v[kMaxEp + 1];
@@ -31,18 +31,23 @@ __device__ __forceinline__ int dest_of(int64_t id, int num_experts, const int32_
   return (d >= 0 && d < ep_size) ? d : -1;
 }
 
-// Single CTA: ordered slots per destination for tokens and routes.  Tokens
-// are taken kPlanThreads at a time (thread = token).  The batch's route
-// destinations are staged in shared memory with coalesced loads; each thread
-// counts its routes per destination, and one block-wide exclusive scan of
-// all destinations at once (token sends in the high 16 bits, routes in the
-// low 16) gives the token's slot and its first route slot per destination,
-// in token order (routes: token-major, then slot, i.e. route order).
+// Ordered slots per destination for tokens and routes, one CTA per
+// kPlanThreads tokens (thread = token).  A CTA first counts, per destination,
+// the tokens and routes of every token before its range (each CTA reads that
+// prefix of the route array itself, so the CTAs need not communicate), then
+// stages its own routes' destinations in shared memory with coalesced loads;
+// each thread counts its routes per destination, and one block-wide exclusive
+// scan of all destinations at once (token sends in the high 16 bits, routes
+// in the low 16) gives the token's slot and its first route slot per
+// destination, in token order (routes: token-major, then slot, i.e. route
+// order) -- the slots of a single pass over the whole batch.  The last CTA
+// writes the totals.
 __global__ void __launch_bounds__(kPlanThreads) ep_plan_kernel(
     const int64_t *__restrict__ ids, int64_t num_tokens, int top_k, int num_experts,
     const int32_t *__restrict__ owner, int ep_size, int32_t *__restrict__ send_token_slot,
     int32_t *__restrict__ route_dest_slot, int32_t *__restrict__ counts) {
   constexpr int kWarps = kPlanThreads / 32;
+  static_assert(kWarps >= kMaxEp, "one warp per destination in the cross-warp scan");
   __shared__ int32_t warp_tot[kWarps][kMaxEp];  // per-warp sums, then warp offsets
   __shared__ int32_t batch_tot[kMaxEp];
   __shared__ int32_t run_tok[kMaxEp];
@@ -57,82 +62,107 @@ __global__ void __launch_bounds__(kPlanThreads) ep_plan_kernel(
     run_rt[tid] = 0;
   }
   __syncthreads();
-  for (int64_t t0 = 0; t0 < num_tokens; t0 += kPlanThreads) {
-    const int64_t t = t0 + tid;
-    const bool valid = t < num_tokens;
-    const int64_t r0 = t0 * top_k;
-    const int64_t nr = min64(num_tokens - t0, kPlanThreads) * top_k;
-    for (int64_t i = tid; i < nr; i += kPlanThreads)
-      s_dest[i] = static_cast<int8_t>(dest_of(ids[r0 + i], num_experts, owner, N));
-    __syncthreads();
-    const int8_t *my_dest = s_dest + static_cast<int64_t>(tid) * top_k;
-    // Per destination: routes (low 16 bits, <= kPlanThreads * 32 in a batch)
-    // and the token itself (high bits).
-    int32_t v[kMaxEp];
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kPlanThreads;
+
+  // Tokens and routes per destination before this CTA's range.
+  {
+    int32_t tok_c[kMaxEp], rt_c[kMaxEp];
 #pragma unroll
-    for (int d = 0; d < kMaxEp; ++d) v[d] = 0;
-    if (valid)
-      for (int s = 0; s < top_k; ++s) {
-        const int ds = my_dest[s];
+    for (int d = 0; d < kMaxEp; ++d) tok_c[d] = rt_c[d] = 0;
+    for (int64_t t = tid; t < t0; t += kPlanThreads) {
+      int32_t v[kMaxEp];
+#pragma unroll
+      for (int d = 0; d < kMaxEp; ++d) v[d] = 0;
+      for (int s2 = 0; s2 < top_k; ++s2) {
+        const int ds = dest_of(ids[t * top_k + s2], num_experts, owner, N);
 #pragma unroll
         for (int d = 0; d < kMaxEp; ++d) v[d] += ds == d ? 1 : 0;
       }
 #pragma unroll
-    for (int d = 0; d < kMaxEp; ++d) v[d] |= (v[d] > 0 ? 1 : 0) << 16;
-    int32_t incl[kMaxEp];
+      for (int d = 0; d < kMaxEp; ++d) {
+        tok_c[d] += v[d] > 0 ? 1 : 0;
+        rt_c[d] += v[d];
+      }
+    }
 #pragma unroll
     for (int d = 0; d < kMaxEp; ++d) {
-      int32_t x = v[d];
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const int32_t u = __shfl_up_sync(0xffffffffu, x, off);
-        if (lane >= off) x += u;
+      const int32_t tk = __reduce_add_sync(0xffffffffu, tok_c[d]);
+      const int32_t rt = __reduce_add_sync(0xffffffffu, rt_c[d]);
+      if (lane == 0 && d < N && (tk | rt)) {
+        atomicAdd(&run_tok[d], tk);
+        atomicAdd(&run_rt[d], rt);
       }
-      incl[d] = x;
     }
-    if (lane == 31) {
-#pragma unroll
-      for (int d = 0; d < kMaxEp; ++d) warp_tot[warp][d] = incl[d];
-    }
-    __syncthreads();
-    if (warp < N) {  // warp d scans destination d across the kWarps warps
-      const int32_t w = warp_tot[lane][warp];
-      int32_t wi = w;
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const int32_t u = __shfl_up_sync(0xffffffffu, wi, off);
-        if (lane >= off) wi += u;
-      }
-      warp_tot[lane][warp] = wi - w;
-      if (lane == 31) batch_tot[warp] = wi;
-    }
-    __syncthreads();
-    if (valid) {
-#pragma unroll
-      for (int d = 0; d < kMaxEp; ++d) {
-        if (d >= N) break;
-        const int32_t before = warp_tot[warp][d] + incl[d] - v[d];
-        const int32_t c = v[d] & 0xffff;
-        send_token_slot[t * N + d] = c > 0 ? run_tok[d] + (before >> 16) : -1;
-        int32_t slot = run_rt[d] + (before & 0xffff);
-        if (c > 0)
-          for (int s = 0; s < top_k; ++s)
-            if (my_dest[s] == d) route_dest_slot[t * top_k + s] = slot++;
-      }
-      // Routes to no rank (dropped or invalid ids).
-      for (int s = 0; s < top_k; ++s)
-        if (my_dest[s] < 0) route_dest_slot[t * top_k + s] = -1;
-    }
-    __syncthreads();
-    if (tid < N) {
-      run_tok[tid] += batch_tot[tid] >> 16;
-      run_rt[tid] += batch_tot[tid] & 0xffff;
-    }
-    __syncthreads();  // s_dest, warp_tot and the running offsets are reused
   }
-  if (tid < N) {
-    counts[tid] = run_tok[tid];
-    counts[N + tid] = run_rt[tid];
+
+  const int64_t t = t0 + tid;
+  const bool valid = t < num_tokens;
+  const int64_t r0 = t0 * top_k;
+  const int64_t nr = min64(num_tokens - t0, kPlanThreads) * top_k;
+  for (int64_t i = tid; i < nr; i += kPlanThreads)
+    s_dest[i] = static_cast<int8_t>(dest_of(ids[r0 + i], num_experts, owner, N));
+  __syncthreads();
+  const int8_t *my_dest = s_dest + static_cast<int64_t>(tid) * top_k;
+  // Per destination: routes (low 16 bits, <= kPlanThreads * 32 in a batch)
+  // and the token itself (high bits).
+  int32_t v[kMaxEp];
+#pragma unroll
+  for (int d = 0; d < kMaxEp; ++d) v[d] = 0;
+  if (valid)
+    for (int s2 = 0; s2 < top_k; ++s2) {
+      const int ds = my_dest[s2];
+#pragma unroll
+      for (int d = 0; d < kMaxEp; ++d) v[d] += ds == d ? 1 : 0;
+    }
+#pragma unroll
+  for (int d = 0; d < kMaxEp; ++d) v[d] |= (v[d] > 0 ? 1 : 0) << 16;
+  int32_t incl[kMaxEp];
+#pragma unroll
+  for (int d = 0; d < kMaxEp; ++d) {
+    int32_t x = v[d];
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int32_t u = __shfl_up_sync(0xffffffffu, x, off);
+      if (lane >= off) x += u;
+    }
+    incl[d] = x;
+  }
+  if (lane == 31) {
+#pragma unroll
+    for (int d = 0; d < kMaxEp; ++d) warp_tot[warp][d] = incl[d];
+  }
+  __syncthreads();
+  if (warp < N) {  // warp d scans destination d across the kWarps warps
+    const int32_t w = lane < kWarps ? warp_tot[lane][warp] : 0;
+    int32_t wi = w;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int32_t u = __shfl_up_sync(0xffffffffu, wi, off);
+      if (lane >= off) wi += u;
+    }
+    if (lane < kWarps) warp_tot[lane][warp] = wi - w;
+    if (lane == 31) batch_tot[warp] = wi;
+  }
+  __syncthreads();
+  if (valid) {
+#pragma unroll
+    for (int d = 0; d < kMaxEp; ++d) {
+      if (d >= N) break;
+      const int32_t before = warp_tot[warp][d] + incl[d] - v[d];
+      const int32_t c = v[d] & 0xffff;
+      send_token_slot[t * N + d] = c > 0 ? run_tok[d] + (before >> 16) : -1;
+      int32_t slot = run_rt[d] + (before & 0xffff);
+      if (c > 0)
+        for (int s2 = 0; s2 < top_k; ++s2)
+          if (my_dest[s2] == d) route_dest_slot[t * top_k + s2] = slot++;
+    }
+    // Routes to no rank (dropped or invalid ids).
+    for (int s2 = 0; s2 < top_k; ++s2)
+      if (my_dest[s2] < 0) route_dest_slot[t * top_k + s2] = -1;
+  }
+  if (blockIdx.x == gridDim.x - 1 && tid < N) {
+    counts[tid] = run_tok[tid] + (batch_tot[tid] >> 16);
+    counts[N + tid] = run_rt[tid] + (batch_tot[tid] & 0xffff);
   }
 }
 
@@ -221,8 +251,11 @@ int b200moe_ep_plan(const int64_t *expert_ids, int64_t num_tokens, int top_k, in
     return B200MOE_OK;
   }
   B200_ARG(expert_ids && send_token_slot && route_dest_slot, "null pointer argument");
-  ep_plan_kernel<<<1, kPlanThreads, 0, s>>>(expert_ids, num_tokens, top_k, num_experts, owner,
-                                            ep_size, send_token_slot, route_dest_slot, counts);
+  const int64_t blocks = (num_tokens + kPlanThreads - 1) / kPlanThreads;
+  B200_ARG(blocks < (int64_t)0x7fffffff, "num_tokens out of range");
+  ep_plan_kernel<<<static_cast<unsigned>(blocks), kPlanThreads, 0, s>>>(
+      expert_ids, num_tokens, top_k, num_experts, owner, ep_size, send_token_slot,
+      route_dest_slot, counts);
   B200_LAUNCHED();
   return B200MOE_OK;
 }

@@ -290,7 +290,8 @@ def test_tall_tiles_equal_wide_tiles_bit_for_bit(shape, tokens, kind):
 
 
 @pytest.mark.parametrize("tokens,top_k,ep_size", [(1, 8, 2), (300, 8, 4), (4096, 8, 8),
-                                                   (2500, 2, 16), (1030, 32, 3)])
+                                                   (2500, 2, 16), (1030, 32, 3), (8192, 8, 8),
+                                                   (512, 8, 8), (513, 8, 5)])
 def test_ep_plan_slots_match_cpu_plan(tokens, top_k, ep_size):
     """Per-destination token and route slots (token order, route order) and
     the counts, against the CPU restatement; includes invalid ids."""
