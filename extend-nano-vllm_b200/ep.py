@@ -293,8 +293,11 @@ class NvlinkExchange:
         layer.ep_all_to_all_count += 1
         layer.total_assignment_count += self.ids.numel()
 
-    def _route_bound(self) -> int:
-        """Host bound on the routes this rank can receive in this call."""
+    def _route_bound(self, assume_equal: bool = True) -> int:
+        """Host bound on the routes this rank can receive in this call.
+        ``assume_equal``: without coordinated counts or a per-peer bound,
+        assume every peer holds as many tokens as this rank (the captured
+        graphs' contract); otherwise fall back to the buffer's capacity."""
         layer = self.layer
         counts = dist_env.get_context().moe_token_counts
         peer_cap = getattr(layer, "nvl_graph_peer_tokens", None)
@@ -302,8 +305,10 @@ class NvlinkExchange:
             tokens = sum(counts)
         elif peer_cap is not None:
             tokens = self.tokens + (layer.ep_size - 1) * max(int(peer_cap), self.tokens)
-        else:
+        elif assume_equal:
             tokens = layer.ep_size * self.tokens
+        else:
+            return self.bufs.max_routes
         per_token = min(layer.top_k, layer.num_local_experts)
         return max(1, min(self.bufs.max_routes, tokens * per_token))
 
@@ -312,8 +317,12 @@ class NvlinkExchange:
         layer, ops, bufs = self.layer, self.layer._ops, self.bufs
         ids, token_of_route, weights, src_rank, src_route, count = ops.nvl_receive(
             layer.ep_rank, bufs)
-        if self.capturing:
-            bound = self._route_bound()
+        # Device-side sizes (no host read) under capture, and eagerly when
+        # the layer asks for them: the host then never waits for the exchange.
+        device_sizes = self.capturing or (getattr(layer, "nvl_eager_device_sizes", False)
+                                          and getattr(ops, "NVL_DIRECT_RETURN", False))
+        if device_sizes:
+            bound = self._route_bound(assume_equal=self.capturing)
             packed = layer._pack(ids[:bound], None, stats=self.stats, route_count=count)
             hint = self.tokens * layer.top_k
             weights = weights[:bound]

@@ -288,6 +288,13 @@ class ExpertParallelMoE(nn.Module):
         # graph size) to let ranks replay graphs of different batch sizes in
         # the same step.
         self.nvl_graph_peer_tokens: int | None = None
+        # Eager calls of the NVLink exchange read the received route count
+        # once per layer and size the temporaries exactly.  True (or
+        # B200MOE_NVL_EAGER_DEVICE_SIZES=1): size them from host bounds and
+        # keep the count on the device, as under graph capture -- no host
+        # read per layer, more memory for the temporaries.
+        self.nvl_eager_device_sizes = (
+            os.environ.get("B200MOE_NVL_EAGER_DEVICE_SIZES", "0") == "1")
         # Counters fed by kernels: host part + device accumulator
         # [local kept routes, dropped routes, dispatched tokens], read
         # (synchronising) on access.

@@ -86,15 +86,18 @@ CASES = [(2, (96, 160), {}), (4, (64, 1, 0, 300), {}), (2, (512, 512), {}),
          (2, (64, 200), {"expert_capacity": 12}), (8, (16,) * 8, {})]
 
 
-@pytest.mark.parametrize("direct", [True, False], ids=["epilogue-return", "copy-return"])
+@pytest.mark.parametrize("mode", ["epilogue-return", "copy-return", "device-sizes"])
 @pytest.mark.parametrize("world,counts,kw", CASES)
 @torch.inference_mode()
-def test_exchange_matches_single_gpu_layer(world, counts, kw, direct, monkeypatch):
-    """``direct``: the down GEMM writes the returned rows into the sources'
-    buffers (default) or y is copied there afterwards."""
+def test_exchange_matches_single_gpu_layer(world, counts, kw, mode, monkeypatch):
+    """Returned rows written by the down GEMM into the sources' buffers
+    (default) or copied there afterwards; eager temporaries sized exactly
+    (default) or from host bounds with the received count on the device."""
     from extend_nano_vllm_b200 import ops
-    monkeypatch.setattr(ops, "NVL_DIRECT_RETURN", direct)
+    monkeypatch.setattr(ops, "NVL_DIRECT_RETURN", mode != "copy-return")
     full, ranks = _layers(world, kw)
+    for layer in ranks:
+        layer.nvl_eager_device_sizes = mode == "device-sizes"
     bufs = _buffers(ranks, max(counts))
     dist_env.set_moe_token_counts(counts)
     for step in range(2):  # the second call reuses the buffers (epoch 2)
