@@ -102,13 +102,16 @@ def parse_args():
     p.add_argument("--no-reference-triton", action="store_true",
                    help="skip timing the reference's own GPU path (baseline/_ref): its Triton "
                         "path at N=1, its expert-parallel backends at N>1")
-    p.add_argument("--profile-case", choices=("gemm-small", "decode", "prefill"), default=None,
+    p.add_argument("--profile-case", choices=("gemm-small", "decode", "prefill", "ep-emulated"),
+                   default=None,
                    help="run a case for ncu captures and exit (no JSON line): gemm-small = "
                         "235B-shaped experts, 16 experts x 320 routed rows, 604 MB of "
                         "weights (larger than L2), --steps forwards; decode = the 30B-A3B "
                         "decode bucket of --profile-tokens tokens captured in a CUDA graph "
                         "and replayed --steps times; prefill = the T=8192 Zipf prefill "
-                        "case, --steps forwards")
+                        "case, --steps forwards; ep-emulated = the NVLink exchange of "
+                        "--profile-ep ranks (235B shape, 4096 tokens each) all on this GPU, "
+                        "phase by phase, --steps exchanges")
     p.add_argument("--engine", default="auto",
                    choices=("auto", "tcgen05", "tcgen05-wide", "tcgen05-tall", "tcgen05-pair"),
                    help="expert GEMM engine of the headline layer (default: the library's choice)")
@@ -122,6 +125,7 @@ def parse_args():
     p.add_argument("--e2e-output", type=int, default=256)
     p.add_argument("--e2e-layers", type=int, default=48)
     p.add_argument("--profile-tokens", type=int, default=1)
+    p.add_argument("--profile-ep", type=int, default=8)
     p.add_argument("--profile-engine", default="auto",
                    choices=("auto", "tcgen05-wide", "tcgen05-swap", "tcgen05-pair",
                             "tcgen05-tall"),
@@ -153,6 +157,32 @@ def profile_case(args) -> None:
             graph.replay()
         torch.cuda.synchronize()
         print(f"profile case decode T={t}: {args.steps} graph replays", flush=True)
+        return
+    if args.profile_case == "ep-emulated":
+        # Every rank's buffers and layer on this GPU; each phase runs for all
+        # ranks before the next phase starts, so every wait is already
+        # satisfied (the kernels and per-rank sizes of an EP step without
+        # the NVLink transfer times).
+        from extend_nano_vllm_b200.ep import NvlinkExchange
+        from extend_nano_vllm_b200.nvl import ExchangeBuffers
+
+        shape, world = wl.QWEN3_235B_A22B, args.profile_ep
+        ranks = [build_layer(shape, world, r, device) for r in range(world)]
+        bufs = [ExchangeBuffers(ep_size=world, rank=r, max_tokens=TOKENS_PER_GPU,
+                                top_k=shape.top_k, num_experts=shape.num_experts,
+                                num_local_experts=shape.num_experts // world,
+                                hidden=shape.hidden, device=device) for r in range(world)]
+        for b in bufs:
+            b.connect_local(bufs)
+        xs = [wl.hidden_states(TOKENS_PER_GPU, shape.hidden, seed=1000 + r, device=device)
+              for r in range(world)]
+        for _ in range(max(1, args.steps)):
+            steps = [NvlinkExchange(layer, x, b) for layer, x, b in zip(ranks, xs, bufs)]
+            for phase in ("route", "dispatch", "compute", "finish"):
+                for st in steps:
+                    getattr(st, phase)()
+        torch.cuda.synchronize()
+        print(f"profile case ep-emulated: {world} ranks, {args.steps} exchanges", flush=True)
         return
     if args.profile_case == "prefill":
         shape = wl.QWEN3_30B_A3B
